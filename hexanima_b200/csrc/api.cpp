@@ -1,0 +1,1158 @@
+// C ABI of libhxdit.so (declared in include/hxdit.h): handles, device buffers, weight sets, the
+// per-block operator and the chain runner.
+//
+// Block orchestration follows the reference site order:
+//  Anima  mega_block_impl, hexagon/mega/blk.c:148-175 (three sites: self-attn, cross-attn, MLP)
+//  MOSS   mode 0, moss/hexagon/mega/blk.c:234-259 (RMS-mod, LoRA-A, QKV+RMS+RoPE, joint attention,
+//         O + gate, RMS-mod, up_gate + SiTU, down + gate)
+// Fusions relative to the reference: q/k RMS+RoPE run in the QKV GEMM epilogue (blk.c:159-160 ran a
+// separate pass), residual+gate in the O/CO/M2 epilogues, GELU in M1, SiTU in up_gate; q|k|v and
+// ck|cv are one GEMM each; the K=8192 down projection runs as one K loop (blk.c:172-174 split it).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <vector>
+
+#include "../../include/hxdit.h"
+#include "hx_internal.h"
+
+using namespace hx;
+
+namespace {
+
+constexpr size_t kAnimaPackF16 = 138416128u;  // W_TOTAL, hexagon/mega/blk_wlayout.h:15
+constexpr size_t kAnimaModW = 125833216u;     // W_MODW
+constexpr size_t kAnimaGain = 125829120u;     // W_GAIN
+inline size_t wq(size_t x) { return x / 2048u * 1152u; }  // WQ(), blk_wlayout.h:17
+constexpr size_t kMossPack = 135397376u;      // W_TOTAL, moss/hexagon/mega/blk_meta.h:17
+
+struct Weights {
+  int model = 0, D = 0, F = 0, Cd = 0, H = 0, lora = 0;
+  DevMat mats[HX_NMATS];
+  bool has[HX_NMATS] = {};
+  const float* gain = nullptr;
+  const __half* modA = nullptr;
+  const __half* modB = nullptr;
+  std::vector<void*> owned;  // device allocations owned by the handle
+};
+
+struct Buf {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+struct ChainGraph {
+  std::vector<int64_t> key;
+  cudaGraphExec_t exec = nullptr;
+  uint64_t last_use = 0;
+};
+constexpr size_t kMaxGraphs = 16;  // e.g. one per denoising step of a sampler
+
+}  // namespace
+
+struct hx_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = true;
+  int* status = nullptr;  // device word
+  std::map<int, Buf> bufs;
+  std::map<int, std::unique_ptr<Weights>> weights;
+  int next_fd = 1;
+  float* modscratch = nullptr;  // chain modulation vectors
+  size_t modscratch_floats = 0;
+  cudaEvent_t ev[34] = {};
+  std::vector<ChainGraph> graphs;
+  uint64_t graph_clock = 0;
+  std::mutex mu;
+  void drop_graphs() {
+    for (auto& g : graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+    graphs.clear();
+  }
+};
+
+namespace {
+
+#define CK(call)                                  \
+  do {                                            \
+    cudaError_t e_ = (call);                      \
+    if (e_ != cudaSuccess) {                      \
+      if (getenv("HX_DEBUG"))                     \
+        fprintf(stderr, "hxdit: %s:%d %s -> %s\n", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+      return HX_E_CUDA;                           \
+    }                                             \
+  } while (0)
+
+struct DevGuard {
+  int prev = -1;
+  explicit DevGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DevGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+DevMat to_devmat(const hx_mat& m) {
+  DevMat d;
+  d.fmt = m.fmt;
+  d.N = m.n;
+  d.K = m.k;
+  d.group = m.group ? m.group : (m.fmt == HX_FMT_F16 ? 64 : 32);
+  d.w = m.w;
+  d.scale = static_cast<__half*>(m.scale);
+  d.minv = static_cast<__half*>(m.minv);
+  return d;
+}
+
+bool valid_mat(const hx_mat& m) {
+  if (!m.w || m.n <= 0 || m.k <= 0) return false;
+  if (m.fmt != HX_FMT_F16 && !m.scale) return false;
+  if (m.fmt == HX_FMT_Q4A && !m.minv) return false;
+  return m.fmt >= 0 && m.fmt <= 3;
+}
+
+// ---------------------------------------------------------------- pack loading
+int alloc_mat(Weights& W, int slot, int fmt, int N, int K, int group) {
+  DevMat& d = W.mats[slot];
+  d.fmt = fmt;
+  d.N = N;
+  d.K = K;
+  d.group = group;
+  const size_t wbytes = fmt == HX_FMT_F16 ? static_cast<size_t>(N) * K * 2 : static_cast<size_t>(N) * K;
+  void* p = nullptr;
+  CK(cudaMalloc(&p, wbytes));
+  W.owned.push_back(p);
+  d.w = p;
+  if (fmt == HX_FMT_Q8) {
+    void* s = nullptr;
+    CK(cudaMalloc(&s, static_cast<size_t>(K / group) * N * 2));
+    W.owned.push_back(s);
+    d.scale = static_cast<__half*>(s);
+  }
+  W.has[slot] = true;
+  return HX_OK;
+}
+
+// copy `bytes` of the pack at `off` into device staging, then repack `nb x kb` tiles into slot rows
+int repack_into(Weights& W, int slot, const uint8_t* dpack, size_t off, int nb, int kb, bool q8, int row0, int mode,
+                cudaStream_t s) {
+  DevMat& d = W.mats[slot];
+  CK(repack_tiles_launch(dpack + off, nb, kb, q8, d.w, d.scale, row0, d.N, mode, s));
+  return HX_OK;
+}
+
+int load_anima(hx_ctx* h, const uint8_t* pack, size_t bytes, Weights& W) {
+  const bool q8 = bytes == wq(kAnimaGain) + 4096 + (kAnimaPackF16 - kAnimaModW);
+  if (!q8 && bytes != kAnimaPackF16) return HX_E_FORMAT;
+  const int D = 2048, Cd = 1024, F = 8192;
+  W.model = HX_MODEL_ANIMA;
+  W.D = D;
+  W.F = F;
+  W.Cd = Cd;
+  W.H = 16;
+  const int fmt = q8 ? HX_FMT_Q8 : HX_FMT_F16;
+  int rc;
+  if ((rc = alloc_mat(W, HX_W_QKV, fmt, 3 * D, D, 32)) || (rc = alloc_mat(W, HX_W_O, fmt, D, D, 32)) ||
+      (rc = alloc_mat(W, HX_W_CQ, fmt, D, D, 32)) || (rc = alloc_mat(W, HX_W_CKV, fmt, 2 * D, Cd, 32)) ||
+      (rc = alloc_mat(W, HX_W_CO, fmt, D, D, 32)) || (rc = alloc_mat(W, HX_W_M1, fmt, F, D, 32)) ||
+      (rc = alloc_mat(W, HX_W_M2, fmt, D, F, 32)))
+    return rc;
+  uint8_t* dpack = nullptr;
+  CK(cudaMalloc(&dpack, bytes));
+  CK(cudaMemcpyAsync(dpack, pack, bytes, cudaMemcpyHostToDevice, h->stream));
+  // order of export_all.py:9 and offsets of blk_wlayout.h:3-12 (fp16) / WQ() (q8)
+  struct M { size_t off; int slot, nb, kb, row0; };
+  const size_t f16off[10] = {0u, 8388608u, 16777216u, 25165824u, 33554432u, 41943040u, 46137344u, 50331648u,
+                             58720256u, 92274688u};
+  auto O = [&](int i) { return q8 ? wq(f16off[i]) : f16off[i]; };
+  const M list[10] = {{O(0), HX_W_QKV, 64, 64, 0},      {O(1), HX_W_QKV, 64, 64, D},  {O(2), HX_W_QKV, 64, 64, 2 * D},
+                      {O(3), HX_W_O, 64, 64, 0},        {O(4), HX_W_CQ, 64, 64, 0},   {O(5), HX_W_CKV, 64, 32, 0},
+                      {O(6), HX_W_CKV, 64, 32, D},      {O(7), HX_W_CO, 64, 64, 0},   {O(8), HX_W_M1, 256, 64, 0},
+                      {O(9), HX_W_M2, 64, 256, 0}};
+  for (const M& m : list) {
+    if ((rc = repack_into(W, m.slot, dpack, m.off, m.nb, m.kb, q8, m.row0, 0, h->stream))) {
+      cudaFree(dpack);
+      return rc;
+    }
+  }
+  const size_t goff = q8 ? wq(kAnimaGain) : kAnimaGain, moff = q8 ? wq(kAnimaGain) + 4096 : kAnimaModW;
+  float* gain = nullptr;
+  __half *mA = nullptr, *mB = nullptr;
+  CK(cudaMalloc(&gain, 512 * 4));
+  CK(cudaMalloc(&mA, 3ull * 256 * D * 2));
+  CK(cudaMalloc(&mB, 3ull * 6144 * 256 * 2));
+  W.owned.push_back(gain);
+  W.owned.push_back(mA);
+  W.owned.push_back(mB);
+  CK(cudaMemcpyAsync(gain, dpack + goff, 512 * 4, cudaMemcpyDeviceToDevice, h->stream));
+  const size_t sa = 256ull * D * 2, sb = 6144ull * 256 * 2;
+  for (int site = 0; site < 3; ++site) {  // per site: a[256][2048] then b[6144][256] (export_all.py:34-36)
+    CK(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(mA) + site * sa, dpack + moff + site * (sa + sb), sa,
+                       cudaMemcpyDeviceToDevice, h->stream));
+    CK(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(mB) + site * sb, dpack + moff + site * (sa + sb) + sa, sb,
+                       cudaMemcpyDeviceToDevice, h->stream));
+  }
+  W.gain = gain;
+  W.modA = mA;
+  W.modB = mB;
+  CK(cudaStreamSynchronize(h->stream));
+  CK(cudaFree(dpack));
+  return HX_OK;
+}
+
+int load_moss(hx_ctx* h, const uint8_t* pack, size_t bytes, Weights& W) {
+  if (bytes != kMossPack) return HX_E_FORMAT;
+  const int D = 3072, F = 8192;
+  W.model = HX_MODEL_MOSS;
+  W.D = D;
+  W.F = F;
+  W.H = 24;
+  W.lora = 1;
+  int rc;
+  const int K1 = D + 128;
+  if ((rc = alloc_mat(W, HX_W_Q, HX_FMT_Q8, D, K1, 32)) || (rc = alloc_mat(W, HX_W_K, HX_FMT_Q8, D, K1, 32)) ||
+      (rc = alloc_mat(W, HX_W_V, HX_FMT_Q8, D, K1, 32)) || (rc = alloc_mat(W, HX_W_O, HX_FMT_Q8, D, K1, 32)) ||
+      (rc = alloc_mat(W, HX_W_M1, HX_FMT_Q8, 2 * F, K1, 32)) ||
+      (rc = alloc_mat(W, HX_W_M2, HX_FMT_Q8, D, F + 128, 32)) ||
+      (rc = alloc_mat(W, HX_W_AQKV, HX_FMT_Q8, 384, D, 32)) || (rc = alloc_mat(W, HX_W_AO, HX_FMT_Q8, 128, D, 32)) ||
+      (rc = alloc_mat(W, HX_W_AUG, HX_FMT_Q8, 128, D, 32)) || (rc = alloc_mat(W, HX_W_ADN, HX_FMT_Q8, 128, F, 32)))
+    return rc;
+  uint8_t* dpack = nullptr;
+  CK(cudaMalloc(&dpack, bytes));
+  CK(cudaMemcpyAsync(dpack, pack, bytes, cudaMemcpyHostToDevice, h->stream));
+  // offsets of moss/hexagon/mega/blk_meta.h:6-16
+  struct M { size_t off; int slot, nb, kb, mode; };
+  const M list[10] = {{0u, HX_W_Q, 96, 100, 0},          {11059200u, HX_W_K, 96, 100, 0},
+                      {22118400u, HX_W_V, 96, 100, 0},   {33177600u, HX_W_O, 96, 100, 0},
+                      {44236800u, HX_W_M1, 512, 100, 1}, {103219200u, HX_W_M2, 96, 260, 0},
+                      {131973120u, HX_W_AQKV, 12, 96, 0}, {133300224u, HX_W_AO, 4, 96, 0},
+                      {133742592u, HX_W_AUG, 4, 96, 0},  {134184960u, HX_W_ADN, 4, 256, 0}};
+  for (const M& m : list) {
+    if ((rc = repack_into(W, m.slot, dpack, m.off, m.nb, m.kb, true, 0, m.mode, h->stream))) {
+      cudaFree(dpack);
+      return rc;
+    }
+  }
+  float* gain = nullptr;
+  CK(cudaMalloc(&gain, (256 + 2 * D) * 4));
+  W.owned.push_back(gain);
+  CK(cudaMemcpyAsync(gain, dpack + 135364608u, (256 + 2 * D) * 4, cudaMemcpyDeviceToDevice, h->stream));
+  W.gain = gain;
+  CK(cudaStreamSynchronize(h->stream));
+  CK(cudaFree(dpack));
+  return HX_OK;
+}
+
+// ---------------------------------------------------------------- block orchestration
+struct Stage {
+  hx_ctx* h;
+  int ntimes;
+  int ti = 0;
+  int stop;
+  bool stopped = false;
+  // returns true when the caller must stop (meta STOP reached)
+  bool tick() {
+    if (ntimes > 0 && ti < 32) cudaEventRecord(h->ev[ti + 1], h->stream);
+    ++ti;
+    if (stop && ti >= stop) stopped = true;
+    return stopped;
+  }
+};
+
+inline const float* fptr(const uint8_t* blob, int off) { return reinterpret_cast<const float*>(blob + off); }
+inline __half* hptr(uint8_t* blob, int off) { return reinterpret_cast<__half*>(blob + off); }
+
+#define CKL(call)                                   \
+  do {                                              \
+    cudaError_t e_ = (call);                        \
+    if (e_ != cudaSuccess) {                        \
+      if (getenv("HX_DEBUG"))                       \
+        fprintf(stderr, "hxdit: %s:%d %s -> %s\n", __FILE__, __LINE__, #call, cudaGetErrorString(e_)); \
+      return e_ == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA; \
+    }                                               \
+  } while (0)
+
+GemmArgs gargs(hx_ctx* h, const __half* A, int lda, int M, const DevMat* W, int epi) {
+  GemmArgs g;
+  g.A = A;
+  g.lda = lda;
+  g.M = M;
+  g.K1 = W->K;
+  g.W = W;
+  g.epi = epi;
+  g.status = h->status;
+  return g;
+}
+
+int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, const float* mod, Stage& st) {
+  const int D = W.D, F = W.F, Cd = W.Cd, H = W.H;
+  const int T = meta[HX_A_NTOK], C = meta[HX_A_NCTX];
+  const int B = meta[HX_A_BATCH] > 0 ? meta[HX_A_BATCH] : 1;
+  const int rows = B * T;
+  cudaStream_t s = h->stream;
+  float* x = reinterpret_cast<float*>(blob + meta[HX_A_X]);
+  __half* hbuf = hptr(blob, meta[HX_A_H]);
+  __half* qkv = hptr(blob, meta[HX_A_Q]);
+  __half* obuf = hptr(blob, meta[HX_A_O]);
+  __half* mid = hptr(blob, meta[HX_A_MID]);
+  __half* ckv = hptr(blob, meta[HX_A_CK]);
+  const __half* ctx = hptr(blob, meta[HX_A_CTX]);
+  const float* cosT = fptr(blob, meta[HX_A_COS]);
+  const float* sinT = fptr(blob, meta[HX_A_SIN]);
+  const float* gain = W.gain;
+  for (int site = 0; site < 3; ++site) {
+    const float* sh = mod + (site * 3 + 0) * D;
+    const float* sc = mod + (site * 3 + 1) * D;
+    const float* gt = mod + (site * 3 + 2) * D;
+    CKL(lnmod_launch(x, hbuf, rows, D, sh, sc, 0, T, 1e-6f, s));
+    if (st.tick()) return HX_OK;
+    if (site == 0) {
+      GemmArgs g = gargs(h, hbuf, D, rows, &W.mats[HX_W_QKV], EPI_RMS);
+      g.out = qkv;
+      g.ldo = 3 * D;
+      g.gain0 = gain;
+      g.gain1 = gain + 128;
+      g.seg1 = D;
+      g.seg2 = 2 * D;
+      g.rope0 = g.rope1 = 1;
+      g.cosT = cosT;
+      g.sinT = sinT;
+      g.rows_per_img = T;
+      CKL(gemm_launch(g, s));
+      if (st.tick()) return HX_OK;
+      if (st.tick()) return HX_OK;  // rope slot: fused into the QKV epilogue
+      AttnArgs a;
+      a.q = qkv; a.ldq = 3 * D; a.q_col0 = 0;
+      a.k = qkv; a.ldk = 3 * D; a.k_col0 = D;
+      a.v = qkv; a.ldv = 3 * D; a.v_col0 = 2 * D;
+      a.o = obuf; a.ldo = D;
+      a.B = B; a.H = H; a.Tq = T; a.Tk = T;
+      a.status = h->status;
+      CKL(attn_launch(a, s));
+      if (st.tick()) return HX_OK;
+      GemmArgs go = gargs(h, obuf, D, rows, &W.mats[HX_W_O], EPI_RESID);
+      go.x = x;
+      go.ldx = D;
+      go.gate = gt;
+      CKL(gemm_launch(go, s));
+      if (st.tick()) return HX_OK;
+    } else if (site == 1) {
+      GemmArgs gq = gargs(h, hbuf, D, rows, &W.mats[HX_W_CQ], EPI_RMS);
+      gq.out = qkv;
+      gq.ldo = 3 * D;
+      gq.gain0 = gain + 256;
+      gq.seg1 = gq.seg2 = D;
+      CKL(gemm_launch(gq, s));
+      GemmArgs gk = gargs(h, ctx, Cd, B * C, &W.mats[HX_W_CKV], EPI_RMS);
+      gk.out = ckv;
+      gk.ldo = 2 * D;
+      gk.gain0 = gain + 384;
+      gk.seg1 = gk.seg2 = D;
+      CKL(gemm_launch(gk, s));
+      if (st.tick()) return HX_OK;
+      if (st.tick()) return HX_OK;  // rms slot: fused into the two GEMMs above
+      AttnArgs a;
+      a.q = qkv; a.ldq = 3 * D; a.q_col0 = 0;
+      a.k = ckv; a.ldk = 2 * D; a.k_col0 = 0;
+      a.v = ckv; a.ldv = 2 * D; a.v_col0 = D;
+      a.o = obuf; a.ldo = D;
+      a.B = B; a.H = H; a.Tq = T; a.Tk = C;
+      a.status = h->status;
+      CKL(attn_launch(a, s));
+      if (st.tick()) return HX_OK;
+      GemmArgs go = gargs(h, obuf, D, rows, &W.mats[HX_W_CO], EPI_RESID);
+      go.x = x;
+      go.ldx = D;
+      go.gate = gt;
+      CKL(gemm_launch(go, s));
+      if (st.tick()) return HX_OK;
+    } else {
+      GemmArgs g1 = gargs(h, hbuf, D, rows, &W.mats[HX_W_M1], EPI_GELU);
+      g1.out = mid;
+      g1.ldo = F;
+      CKL(gemm_launch(g1, s));
+      if (st.tick()) return HX_OK;
+      GemmArgs g2 = gargs(h, mid, F, rows, &W.mats[HX_W_M2], EPI_RESID);
+      g2.x = x;
+      g2.ldx = D;
+      g2.gate = gt;
+      CKL(gemm_launch(g2, s));
+      if (st.tick()) return HX_OK;
+    }
+  }
+  return HX_OK;
+}
+
+int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, const float* mod, Stage& st) {
+  const int D = W.D, F = W.F, H = W.H;
+  const int T = meta[HX_S_NTOK];
+  const int nvalid = meta[HX_S_NVALID] > 0 ? meta[HX_S_NVALID] : T;
+  const int B = meta[HX_S_BATCH] > 0 ? meta[HX_S_BATCH] : 1;
+  if (meta[HX_S_MODE] != 0) return HX_E_ARG;  // text-refiner / projection modes are not built
+  const int rows = B * T;
+  cudaStream_t s = h->stream;
+  float* x = reinterpret_cast<float*>(blob + meta[HX_S_X]);
+  __half* hbuf = hptr(blob, meta[HX_S_H]);
+  __half* qkv = hptr(blob, meta[HX_S_Q]);
+  __half* obuf = hptr(blob, meta[HX_S_O]);
+  __half* mid = hptr(blob, meta[HX_S_MID]);
+  const float* cosT = fptr(blob, meta[HX_S_COS]);
+  const float* sinT = fptr(blob, meta[HX_S_SIN]);
+  const float* gain = W.gain;
+  const float *sh_a = mod, *sc_a = mod + D, *gt_a = mod + 2 * D, *sh_f = mod + 3 * D, *sc_f = mod + 4 * D,
+              *gt_f = mod + 5 * D;
+  const bool lora = W.lora != 0;
+  __half *lq = nullptr, *lo = nullptr, *lu = nullptr, *ld = nullptr;
+  if (lora) {
+    lq = hptr(blob, meta[HX_S_LQ]);
+    lo = hptr(blob, meta[HX_S_LO]);
+    lu = hptr(blob, meta[HX_S_LU]);
+    ld = hptr(blob, meta[HX_S_LD]);
+  }
+  // ---- attention half
+  CKL(rmsmod_launch(x, hbuf, rows, D, gain + 256, sh_a, sc_a, 0, T, 1e-6f, s));
+  if (st.tick()) return HX_OK;
+  if (lora) {
+    GemmArgs ga = gargs(h, hbuf, D, rows, &W.mats[HX_W_AQKV], EPI_STORE);
+    ga.out = lq;
+    ga.ldo = 384;
+    CKL(gemm_launch(ga, s));
+  }
+  if (st.tick()) return HX_OK;
+  if (lora) {
+    const int slots[3] = {HX_W_Q, HX_W_K, HX_W_V};
+    for (int j = 0; j < 3; ++j) {
+      GemmArgs g = gargs(h, hbuf, D, rows, &W.mats[slots[j]], j < 2 ? EPI_RMS : EPI_STORE);
+      g.K1 = D;
+      g.A2 = lq + 128 * j;
+      g.lda2 = 384;
+      g.out = qkv + j * D;
+      g.ldo = 3 * D;
+      g.gain0 = gain + 128 * j;
+      g.seg1 = g.seg2 = D;
+      g.rope0 = 1;
+      g.cosT = cosT;
+      g.sinT = sinT;
+      g.rows_per_img = T;
+      CKL(gemm_launch(g, s));
+    }
+  } else {
+    GemmArgs g = gargs(h, hbuf, D, rows, &W.mats[HX_W_QKV], EPI_RMS);
+    g.out = qkv;
+    g.ldo = 3 * D;
+    g.gain0 = gain;
+    g.gain1 = gain + 128;
+    g.seg1 = D;
+    g.seg2 = 2 * D;
+    g.rope0 = g.rope1 = 1;
+    g.cosT = cosT;
+    g.sinT = sinT;
+    g.rows_per_img = T;
+    CKL(gemm_launch(g, s));
+  }
+  if (st.tick()) return HX_OK;
+  AttnArgs a;
+  a.q = qkv; a.ldq = 3 * D; a.q_col0 = 0;
+  a.k = qkv; a.ldk = 3 * D; a.k_col0 = D;
+  a.v = qkv; a.ldv = 3 * D; a.v_col0 = 2 * D;
+  a.o = obuf; a.ldo = D;
+  a.B = B; a.H = H; a.Tq = T; a.Tk = T; a.nvalid = nvalid;
+  a.status = h->status;
+  CKL(attn_launch(a, s));
+  if (st.tick()) return HX_OK;
+  {
+    if (lora) {
+      GemmArgs ga = gargs(h, obuf, D, rows, &W.mats[HX_W_AO], EPI_STORE);
+      ga.out = lo;
+      ga.ldo = 128;
+      CKL(gemm_launch(ga, s));
+    }
+    GemmArgs g = gargs(h, obuf, D, rows, &W.mats[HX_W_O], EPI_RESID);
+    if (lora) {
+      g.K1 = D;
+      g.A2 = lo;
+      g.lda2 = 128;
+    }
+    g.x = x;
+    g.ldx = D;
+    g.gate = gt_a;
+    CKL(gemm_launch(g, s));
+  }
+  if (st.tick()) return HX_OK;
+  // ---- FFN half
+  CKL(rmsmod_launch(x, hbuf, rows, D, gain + 256 + D, sh_f, sc_f, 0, T, 1e-6f, s));
+  if (st.tick()) return HX_OK;
+  {
+    if (lora) {
+      GemmArgs ga = gargs(h, hbuf, D, rows, &W.mats[HX_W_AUG], EPI_STORE);
+      ga.out = lu;
+      ga.ldo = 128;
+      CKL(gemm_launch(ga, s));
+    }
+    GemmArgs g = gargs(h, hbuf, D, rows, &W.mats[HX_W_M1], EPI_SITU);
+    if (lora) {
+      g.K1 = D;
+      g.A2 = lu;
+      g.lda2 = 128;
+    }
+    g.out = mid;
+    g.ldo = F;
+    CKL(gemm_launch(g, s));
+  }
+  if (st.tick()) return HX_OK;
+  {
+    if (lora) {
+      GemmArgs ga = gargs(h, mid, F, rows, &W.mats[HX_W_ADN], EPI_STORE);
+      ga.out = ld;
+      ga.ldo = 128;
+      CKL(gemm_launch(ga, s));
+    }
+    GemmArgs g = gargs(h, mid, F, rows, &W.mats[HX_W_M2], EPI_RESID);
+    if (lora) {
+      g.K1 = F;
+      g.A2 = ld;
+      g.lda2 = 128;
+    }
+    g.x = x;
+    g.ldx = D;
+    g.gate = gt_f;
+    CKL(gemm_launch(g, s));
+  }
+  st.tick();
+  return HX_OK;
+}
+
+// bytes the block reads/writes through meta offsets; checks they stay inside the blob
+int check_meta(const Weights& W, const int32_t* meta, int nmeta, size_t blob_bytes) {
+  auto in = [&](int off, size_t bytes) {
+    return off >= 0 && static_cast<size_t>(off) <= blob_bytes && bytes <= blob_bytes - off;
+  };
+  if (W.model == HX_MODEL_ANIMA) {
+    if (nmeta < HX_A_NMETA) return HX_E_ARG;
+    const size_t T = meta[HX_A_NTOK], C = meta[HX_A_NCTX];
+    const size_t B = (nmeta > HX_A_BATCH && meta[HX_A_BATCH] > 0) ? meta[HX_A_BATCH] : 1;
+    if (T == 0 || T % 32 || C == 0 || C % 32) return HX_E_ARG;
+    const size_t D = W.D, F = W.F, R = B * T;
+    if (!in(meta[HX_A_X], R * D * 4) || !in(meta[HX_A_CTX], B * C * W.Cd * 2) || !in(meta[HX_A_COS], T * 256) ||
+        !in(meta[HX_A_SIN], T * 256) || !in(meta[HX_A_H], R * D * 2) || !in(meta[HX_A_Q], R * 3 * D * 2) ||
+        !in(meta[HX_A_O], R * D * 2) || !in(meta[HX_A_MID], R * F * 2) || !in(meta[HX_A_CK], B * C * 2 * D * 2))
+      return HX_E_RANGE;
+    for (int slot : {HX_A_X, HX_A_CTX, HX_A_COS, HX_A_SIN, HX_A_H, HX_A_Q, HX_A_O, HX_A_MID, HX_A_CK})
+      if (meta[slot] % 256) return HX_E_RANGE;
+  } else {
+    if (nmeta < HX_S_NMETA) return HX_E_ARG;
+    const size_t T = meta[HX_S_NTOK];
+    const size_t B = (nmeta > HX_S_BATCH && meta[HX_S_BATCH] > 0) ? meta[HX_S_BATCH] : 1;
+    if (T == 0 || T % 32) return HX_E_ARG;
+    if (meta[HX_S_NVALID] < 0 || static_cast<size_t>(meta[HX_S_NVALID]) > T) return HX_E_ARG;
+    const size_t D = W.D, F = W.F, R = B * T;
+    if (!in(meta[HX_S_X], R * D * 4) || !in(meta[HX_S_COS], T * 256) || !in(meta[HX_S_SIN], T * 256) ||
+        !in(meta[HX_S_H], R * D * 2) || !in(meta[HX_S_Q], R * 3 * D * 2) || !in(meta[HX_S_O], R * D * 2) ||
+        !in(meta[HX_S_MID], R * F * 2))
+      return HX_E_RANGE;
+    if (W.lora && (!in(meta[HX_S_LQ], R * 384 * 2) || !in(meta[HX_S_LO], R * 256) || !in(meta[HX_S_LU], R * 256) ||
+                   !in(meta[HX_S_LD], R * 256)))
+      return HX_E_RANGE;
+    for (int slot : {HX_S_X, HX_S_COS, HX_S_SIN, HX_S_H, HX_S_Q, HX_S_O, HX_S_MID})
+      if (meta[slot] % 256) return HX_E_RANGE;
+  }
+  return HX_OK;
+}
+
+int run_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, const float* mod_dev, Stage& st) {
+  return W.model == HX_MODEL_ANIMA ? anima_block(h, W, meta, blob, mod_dev, st)
+                                   : moss_block(h, W, meta, blob, mod_dev, st);
+}
+
+std::vector<int32_t> full_meta(const int32_t* meta, int nmeta, int model) {
+  const int n = model == HX_MODEL_ANIMA ? HX_A_NMETA_EXT : HX_S_NMETA_EXT;
+  std::vector<int32_t> m(std::max(n, nmeta), 0);
+  std::copy(meta, meta + nmeta, m.begin());
+  return m;
+}
+
+hx_ctx* H(hx_handle h) { return reinterpret_cast<hx_ctx*>(h); }
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+const char* hx_version(void) { return "hxdit 0.1 (sm_100a)"; }
+
+int hx_open(int device, hx_handle* out) {
+  if (!out) return HX_E_ARG;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return HX_E_ARG;
+  DevGuard g(device);
+  auto* h = new hx_ctx();
+  h->device = device;
+  if (cudaStreamCreateWithFlags(&h->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&h->status, sizeof(int)) != cudaSuccess || cudaMemset(h->status, 0, sizeof(int)) != cudaSuccess) {
+    delete h;
+    return HX_E_CUDA;
+  }
+  for (auto& e : h->ev) cudaEventCreate(&e);
+  *out = reinterpret_cast<hx_handle>(h);
+  return HX_OK;
+}
+
+int hx_close(hx_handle hh) {
+  hx_ctx* h = H(hh);
+  if (!h) return HX_E_ARG;
+  {
+    DevGuard g(h->device);
+    cudaStreamSynchronize(h->stream);
+    h->drop_graphs();
+    for (auto& kv : h->bufs) cudaFree(kv.second.ptr);
+    for (auto& kv : h->weights)
+      for (void* p : kv.second->owned) cudaFree(p);
+    cudaFree(h->modscratch);
+    cudaFree(h->status);
+    for (auto& e : h->ev) cudaEventDestroy(e);
+    if (h->own_stream) cudaStreamDestroy(h->stream);
+  }
+  delete h;
+  return HX_OK;
+}
+
+int hx_get_stream(hx_handle hh, void** stream) {
+  if (!hh || !stream) return HX_E_ARG;
+  *stream = H(hh)->stream;
+  return HX_OK;
+}
+
+int hx_set_stream(hx_handle hh, void* stream) {
+  hx_ctx* h = H(hh);
+  if (!h) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  DevGuard g(h->device);
+  cudaStreamSynchronize(h->stream);
+  if (h->own_stream) cudaStreamDestroy(h->stream);
+  h->stream = static_cast<cudaStream_t>(stream);
+  h->own_stream = false;
+  h->drop_graphs();
+  return HX_OK;
+}
+
+int hx_sync(hx_handle hh) {
+  hx_ctx* h = H(hh);
+  if (!h) return HX_E_ARG;
+  DevGuard g(h->device);
+  CK(cudaStreamSynchronize(h->stream));
+  return HX_OK;
+}
+
+int hx_status(hx_handle hh, int* status) {
+  hx_ctx* h = H(hh);
+  if (!h || !status) return HX_E_ARG;
+  DevGuard g(h->device);
+  CK(cudaStreamSynchronize(h->stream));
+  CK(cudaMemcpy(status, h->status, sizeof(int), cudaMemcpyDeviceToHost));
+  CK(cudaMemset(h->status, 0, sizeof(int)));
+  return HX_OK;
+}
+
+int hx_status_ptr(hx_handle hh, int** status_dev) {
+  if (!hh || !status_dev) return HX_E_ARG;
+  *status_dev = H(hh)->status;
+  return HX_OK;
+}
+
+// ---------------------------------------------------------------- buffers
+int hx_buf_alloc(hx_handle hh, size_t bytes, int* fd) {
+  hx_ctx* h = H(hh);
+  if (!h || !fd || !bytes) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  DevGuard g(h->device);
+  void* p = nullptr;
+  CK(cudaMalloc(&p, bytes));
+  CK(cudaMemsetAsync(p, 0, bytes, h->stream));
+  *fd = h->next_fd++;
+  h->bufs[*fd] = Buf{p, bytes};
+  return HX_OK;
+}
+
+int hx_buf_free(hx_handle hh, int fd) {
+  hx_ctx* h = H(hh);
+  if (!h) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto it = h->bufs.find(fd);
+  if (it == h->bufs.end()) return HX_E_ARG;
+  DevGuard g(h->device);
+  cudaStreamSynchronize(h->stream);
+  cudaFree(it->second.ptr);
+  h->bufs.erase(it);
+  h->drop_graphs();
+  return HX_OK;
+}
+
+int hx_buf_ptr(hx_handle hh, int fd, void** dev) {
+  hx_ctx* h = H(hh);
+  if (!h || !dev) return HX_E_ARG;
+  auto it = h->bufs.find(fd);
+  if (it == h->bufs.end()) return HX_E_ARG;
+  *dev = it->second.ptr;
+  return HX_OK;
+}
+
+int hx_buf_write(hx_handle hh, int fd, size_t off, const void* src, size_t bytes) {
+  hx_ctx* h = H(hh);
+  if (!h || (!src && bytes)) return HX_E_ARG;
+  auto it = h->bufs.find(fd);
+  if (it == h->bufs.end() || off > it->second.bytes || bytes > it->second.bytes - off) return HX_E_ARG;
+  DevGuard g(h->device);
+  CK(cudaMemcpyAsync(static_cast<uint8_t*>(it->second.ptr) + off, src, bytes, cudaMemcpyHostToDevice, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return HX_OK;
+}
+
+int hx_buf_read(hx_handle hh, int fd, size_t off, void* dst, size_t bytes) {
+  hx_ctx* h = H(hh);
+  if (!h || (!dst && bytes)) return HX_E_ARG;
+  auto it = h->bufs.find(fd);
+  if (it == h->bufs.end() || off > it->second.bytes || bytes > it->second.bytes - off) return HX_E_ARG;
+  DevGuard g(h->device);
+  CK(cudaMemcpyAsync(dst, static_cast<uint8_t*>(it->second.ptr) + off, bytes, cudaMemcpyDeviceToHost, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  return HX_OK;
+}
+
+// ---------------------------------------------------------------- weights
+int hx_weights_load(hx_handle hh, int model, const void* pack, size_t bytes, int* wfd) {
+  hx_ctx* h = H(hh);
+  if (!h || !pack || !wfd) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  DevGuard g(h->device);
+  auto W = std::make_unique<Weights>();
+  int rc = model == HX_MODEL_ANIMA ? load_anima(h, static_cast<const uint8_t*>(pack), bytes, *W)
+           : model == HX_MODEL_MOSS ? load_moss(h, static_cast<const uint8_t*>(pack), bytes, *W)
+                                    : HX_E_ARG;
+  if (rc) {
+    for (void* p : W->owned) cudaFree(p);
+    return rc;
+  }
+  *wfd = h->next_fd++;
+  h->weights[*wfd] = std::move(W);
+  return HX_OK;
+}
+
+int hx_weights_bind(hx_handle hh, const hx_weight_desc* d, int* wfd) {
+  hx_ctx* h = H(hh);
+  if (!h || !d || !wfd) return HX_E_ARG;
+  auto W = std::make_unique<Weights>();
+  W->model = d->model;
+  W->D = d->D;
+  W->F = d->F;
+  W->Cd = d->Cd;
+  W->H = d->H > 0 ? d->H : d->D / 128;
+  W->lora = d->lora;
+  W->gain = d->gain;
+  W->modA = static_cast<const __half*>(d->modA);
+  W->modB = static_cast<const __half*>(d->modB);
+  if (W->D <= 0 || W->D % 128 || W->F <= 0 || W->F % 256 || W->H * 128 != W->D || !W->gain) return HX_E_ARG;
+  std::vector<int> need;
+  if (d->model == HX_MODEL_ANIMA) {
+    need = {HX_W_QKV, HX_W_O, HX_W_CQ, HX_W_CKV, HX_W_CO, HX_W_M1, HX_W_M2};
+    if (W->Cd <= 0 || W->Cd % 64) return HX_E_ARG;
+  } else if (d->model == HX_MODEL_MOSS) {
+    need = d->lora ? std::vector<int>{HX_W_Q, HX_W_K, HX_W_V, HX_W_O, HX_W_M1, HX_W_M2, HX_W_AQKV, HX_W_AO, HX_W_AUG,
+                                      HX_W_ADN}
+                   : std::vector<int>{HX_W_QKV, HX_W_O, HX_W_M1, HX_W_M2};
+  } else {
+    return HX_E_ARG;
+  }
+  for (int slot : need) {
+    if (!valid_mat(d->mats[slot])) return HX_E_ARG;
+    W->mats[slot] = to_devmat(d->mats[slot]);
+    W->has[slot] = true;
+  }
+  std::lock_guard<std::mutex> lk(h->mu);
+  *wfd = h->next_fd++;
+  h->weights[*wfd] = std::move(W);
+  return HX_OK;
+}
+
+int hx_weights_free(hx_handle hh, int wfd) {
+  hx_ctx* h = H(hh);
+  if (!h) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto it = h->weights.find(wfd);
+  if (it == h->weights.end()) return HX_E_NOWEIGHTS;
+  DevGuard g(h->device);
+  cudaStreamSynchronize(h->stream);
+  for (void* p : it->second->owned) cudaFree(p);
+  h->weights.erase(it);
+  h->drop_graphs();
+  return HX_OK;
+}
+
+// ---------------------------------------------------------------- blob layout
+int hx_blob_layout(int model, int ntok, int nctx, int batch, int D, int F, int Cd, int32_t* meta, int nmeta,
+                   size_t* total) {
+  if (!meta || !total || ntok <= 0 || ntok % 32 || batch <= 0 || D <= 0 || F <= 0) return HX_E_ARG;
+  auto up = [](size_t v) { return (v + 4095) & ~size_t(4095); };
+  size_t off = 0;
+  const size_t R = static_cast<size_t>(batch) * ntok;
+  auto place = [&](int slot, size_t bytes) {
+    meta[slot] = static_cast<int32_t>(off);
+    off += up(bytes);
+  };
+  if (model == HX_MODEL_ANIMA) {
+    if (nmeta < HX_A_NMETA_EXT || nctx <= 0 || nctx % 32 || Cd <= 0) return HX_E_ARG;
+    std::fill(meta, meta + nmeta, 0);
+    place(HX_A_X, R * D * 4);
+    place(HX_A_CTX, static_cast<size_t>(batch) * nctx * Cd * 2);
+    place(HX_A_MOD, (9ull * D + 3 * 256) * 4);
+    place(HX_A_COS, static_cast<size_t>(ntok) * 64 * 4);
+    place(HX_A_SIN, static_cast<size_t>(ntok) * 64 * 4);
+    place(HX_A_H, R * D * 2);
+    place(HX_A_Q, R * 3 * D * 2);
+    meta[HX_A_K] = meta[HX_A_Q];
+    meta[HX_A_V] = meta[HX_A_Q];
+    place(HX_A_O, R * D * 2);
+    meta[HX_A_T] = meta[HX_A_O];
+    place(HX_A_MID, R * F * 2);
+    place(HX_A_CK, static_cast<size_t>(batch) * nctx * 2 * D * 2);
+    meta[HX_A_CV] = meta[HX_A_CK];
+    meta[HX_A_NTOK] = ntok;
+    meta[HX_A_NCTX] = nctx;
+    meta[HX_A_REL] = 1;
+    meta[HX_A_FIRST] = 1;
+    meta[HX_A_BATCH] = batch;
+  } else if (model == HX_MODEL_MOSS) {
+    if (nmeta < HX_S_NMETA_EXT) return HX_E_ARG;
+    std::fill(meta, meta + nmeta, 0);
+    place(HX_S_X, R * D * 4);
+    place(HX_S_COS, static_cast<size_t>(ntok) * 64 * 4);
+    place(HX_S_SIN, static_cast<size_t>(ntok) * 64 * 4);
+    place(HX_S_CS, 6ull * D * 4);  // mod vectors when the call passes none
+    place(HX_S_H, R * D * 2);
+    place(HX_S_Q, R * 3 * D * 2);
+    meta[HX_S_K] = meta[HX_S_Q];
+    meta[HX_S_V] = meta[HX_S_Q];
+    place(HX_S_O, R * D * 2);
+    meta[HX_S_T] = meta[HX_S_O];
+    place(HX_S_MID, R * F * 2);
+    place(HX_S_LQ, R * 384 * 2);
+    place(HX_S_LO, R * 128 * 2);
+    place(HX_S_LU, R * 128 * 2);
+    place(HX_S_LD, R * 128 * 2);
+    meta[HX_S_NTOK] = ntok;
+    meta[HX_S_NVALID] = ntok;
+    meta[HX_S_REL] = 1;
+    meta[HX_S_FIRST] = 1;
+    meta[HX_S_NCB] = D / 32;
+    meta[HX_S_BATCH] = batch;
+  } else {
+    return HX_E_ARG;
+  }
+  if (off > 0x7FFFFFFFull) return HX_E_RANGE;  // meta slots are int32 byte offsets, as in the reference
+  *total = off;
+  return HX_OK;
+}
+
+// ---------------------------------------------------------------- per-block operator
+int hx_mega_block(hx_handle hh, const int32_t* meta, int nmeta, int wfd, int bfd, const uint8_t* mod, int modlen,
+                  int32_t* times, int ntimes, int32_t* rc) {
+  hx_ctx* h = H(hh);
+  if (!h || !rc) return HX_E_ARG;
+  const auto t_entry = std::chrono::steady_clock::now();
+  *rc = HX_OK;
+  if (times)
+    for (int i = 0; i < ntimes; ++i) times[i] = 0;
+  if (!meta) return (*rc = HX_E_ARG);
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto wi = h->weights.find(wfd);
+  if (wi == h->weights.end()) return (*rc = HX_E_NOWEIGHTS);
+  auto bi = h->bufs.find(bfd);
+  if (bi == h->bufs.end()) return (*rc = HX_E_NOBLOB);
+  const Weights& W = *wi->second;
+  std::vector<int32_t> m = full_meta(meta, nmeta, W.model);
+  if (int r = check_meta(W, m.data(), static_cast<int>(m.size()), bi->second.bytes)) return (*rc = r);
+  DevGuard g(h->device);
+  uint8_t* blob = static_cast<uint8_t*>(bi->second.ptr);
+  const int D = W.D;
+  const bool anima = W.model == HX_MODEL_ANIMA;
+  const int nmod = anima ? 9 * D : 6 * D;
+  const int modslot = anima ? HX_A_MOD : HX_S_CS;
+  if (anima && m[HX_A_STOP] == 99) return HX_OK;  // reference probe: map weights, do nothing
+  float* mod_dev = reinterpret_cast<float*>(blob + m[modslot]);
+  if (static_cast<size_t>(m[modslot]) + static_cast<size_t>(nmod) * 4 > bi->second.bytes) return (*rc = HX_E_RANGE);
+  if (mod) {
+    if (modlen < nmod * 4) return (*rc = HX_E_ARG);
+    if (cudaMemcpyAsync(mod_dev, mod, static_cast<size_t>(nmod) * 4, cudaMemcpyHostToDevice, h->stream) != cudaSuccess)
+      return (*rc = HX_E_CUDA);
+  }
+  Stage st{h, times ? ntimes : 0, 0, anima ? m[HX_A_STOP] : m[HX_S_STOP]};
+  if (st.ntimes > 0) cudaEventRecord(h->ev[0], h->stream);
+  if (times && ntimes > 24)
+    times[24] = static_cast<int32_t>(
+        std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t_entry).count());
+  int r = run_block(h, W, m.data(), blob, mod_dev, st);
+  if (r) return (*rc = r);
+  if (st.ntimes > 0) {
+    if (cudaStreamSynchronize(h->stream) != cudaSuccess) return (*rc = HX_E_CUDA);
+    for (int i = 0; i < st.ti && i < ntimes && i < 24; ++i) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, h->ev[i], h->ev[i + 1]);
+      times[i] = static_cast<int32_t>(ms * 1000.f);
+    }
+    int stv = 0;
+    cudaMemcpy(&stv, h->status, sizeof(int), cudaMemcpyDeviceToHost);
+    if (stv) {
+      cudaMemset(h->status, 0, sizeof(int));
+      return (*rc = HX_E_TIMEOUT);
+    }
+  }
+  if (cudaPeekAtLastError() != cudaSuccess) return (*rc = HX_E_CUDA);
+  return HX_OK;
+}
+
+int hx_modulation(hx_handle hh, int wfd, const float* emb_dev, const float* lora_dev, float* mod_dev) {
+  hx_ctx* h = H(hh);
+  if (!h || !emb_dev || !mod_dev) return HX_E_ARG;
+  auto wi = h->weights.find(wfd);
+  if (wi == h->weights.end()) return HX_E_NOWEIGHTS;
+  const Weights& W = *wi->second;
+  if (W.model != HX_MODEL_ANIMA || !W.modA || !W.modB) return HX_E_ARG;
+  DevGuard g(h->device);
+  CK(modulation_launch(W.modA, W.modB, emb_dev, lora_dev, mod_dev, 3, W.D, 256, 3 * W.D, h->stream));
+  return HX_OK;
+}
+
+int hx_chain(hx_handle hh, const int32_t* meta, int nmeta, const int* wfds, int count, int bfd, const float* mods_dev,
+             const float* emb_dev, const float* lora_dev, uint32_t skipmask, int use_graph, int32_t* rc) {
+  hx_ctx* h = H(hh);
+  if (!h || !rc || !meta || !wfds || count <= 0) return HX_E_ARG;
+  *rc = HX_OK;
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto bi = h->bufs.find(bfd);
+  if (bi == h->bufs.end()) return (*rc = HX_E_NOBLOB);
+  std::vector<const Weights*> ws(count);
+  for (int k = 0; k < count; ++k) {
+    auto wi = h->weights.find(wfds[k]);
+    if (wi == h->weights.end()) return (*rc = HX_E_NOWEIGHTS);
+    ws[k] = wi->second.get();
+    if (ws[k]->model != ws[0]->model || ws[k]->D != ws[0]->D) return (*rc = HX_E_ARG);
+  }
+  const int model = ws[0]->model, D = ws[0]->D;
+  std::vector<int32_t> m = full_meta(meta, nmeta, model);
+  for (int k = 0; k < count; ++k)
+    if (int r = check_meta(*ws[k], m.data(), static_cast<int>(m.size()), bi->second.bytes)) return (*rc = r);
+  const size_t per = model == HX_MODEL_ANIMA ? 9ull * D + 3 * 256 : 6ull * D;
+  if (!mods_dev) {
+    if (model != HX_MODEL_ANIMA || !emb_dev) return (*rc = HX_E_ARG);
+    for (int k = 0; k < count; ++k)
+      if (!ws[k]->modA || !ws[k]->modB) return (*rc = HX_E_ARG);
+  }
+  DevGuard g(h->device);
+  if (!mods_dev && h->modscratch_floats < per * count) {
+    cudaStreamSynchronize(h->stream);
+    cudaFree(h->modscratch);
+    h->modscratch = nullptr;
+    h->modscratch_floats = 0;
+    if (cudaMalloc(&h->modscratch, per * count * 4) != cudaSuccess) return (*rc = HX_E_CUDA);
+    h->modscratch_floats = per * count;
+    h->drop_graphs();
+  }
+  uint8_t* blob = static_cast<uint8_t*>(bi->second.ptr);
+  auto body = [&]() -> int {
+    for (int k = 0; k < count; ++k) {
+      if ((skipmask >> k) & 1) continue;
+      const float* md;
+      if (mods_dev) {
+        md = mods_dev + static_cast<size_t>(k) * (model == HX_MODEL_ANIMA ? 9 * D : 6 * D);
+      } else {
+        float* out = h->modscratch + per * k;
+        if (modulation_launch(ws[k]->modA, ws[k]->modB, emb_dev, lora_dev, out, 3, D, 256, 3 * D, h->stream) !=
+            cudaSuccess)
+          return HX_E_CUDA;
+        md = out;
+      }
+      Stage st{h, 0, 0, 0};
+      if (int r = run_block(h, *ws[k], m.data(), blob, md, st)) return r;
+    }
+    return HX_OK;
+  };
+  if (!use_graph) {
+    int r = body();
+    return (*rc = r);
+  }
+  std::vector<int64_t> key(m.begin(), m.end());
+  for (int k = 0; k < count; ++k) key.push_back(wfds[k]);
+  key.push_back(bfd);
+  key.push_back(reinterpret_cast<int64_t>(mods_dev));
+  key.push_back(reinterpret_cast<int64_t>(emb_dev));
+  key.push_back(reinterpret_cast<int64_t>(lora_dev));
+  key.push_back(skipmask);
+  key.push_back(reinterpret_cast<int64_t>(h->stream));
+  ChainGraph* hit = nullptr;
+  for (auto& g : h->graphs)
+    if (g.key == key) hit = &g;
+  if (!hit) {
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeRelaxed) != cudaSuccess) return (*rc = HX_E_CUDA);
+    int r = body();
+    cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
+    if (r || ce != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return (*rc = r ? r : HX_E_CUDA);
+    }
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return (*rc = HX_E_CUDA);
+    if (h->graphs.size() >= kMaxGraphs) {  // evict the least recently used
+      auto lru = std::min_element(h->graphs.begin(), h->graphs.end(),
+                                  [](const ChainGraph& a, const ChainGraph& b) { return a.last_use < b.last_use; });
+      cudaGraphExecDestroy(lru->exec);
+      h->graphs.erase(lru);
+    }
+    h->graphs.push_back(ChainGraph{key, exec, 0});
+    hit = &h->graphs.back();
+  }
+  hit->last_use = ++h->graph_clock;
+  if (cudaGraphLaunch(hit->exec, h->stream) != cudaSuccess) return (*rc = HX_E_CUDA);
+  return HX_OK;
+}
+
+// ---------------------------------------------------------------- operator level
+int hx_gemm(hx_handle hh, const hx_gemm_desc* d) {
+  hx_ctx* h = H(hh);
+  if (!h || !d || !valid_mat(d->w)) return HX_E_ARG;
+  DevGuard g(h->device);
+  DevMat W = to_devmat(d->w);
+  GemmArgs a;
+  a.A = static_cast<const __half*>(d->a);
+  a.lda = d->lda;
+  a.A2 = static_cast<const __half*>(d->a2);
+  a.lda2 = d->lda2;
+  a.M = d->m;
+  a.K1 = d->k1 > 0 ? d->k1 : W.K;
+  a.W = &W;
+  a.epi = d->epi;
+  a.out = static_cast<__half*>(d->out);
+  a.ldo = d->ldo;
+  a.x = d->x;
+  a.ldx = d->ldx;
+  a.gate = d->gate;
+  a.vec_bstride = d->vec_bstride;
+  a.rows_per_img = d->rows_per_img > 0 ? d->rows_per_img : (1 << 30);
+  a.gain0 = d->gain0;
+  a.gain1 = d->gain1;
+  a.seg1 = d->seg1;
+  a.seg2 = d->seg2;
+  a.rope0 = d->rope0;
+  a.rope1 = d->rope1;
+  a.cosT = d->cos_t;
+  a.sinT = d->sin_t;
+  a.eps = d->eps > 0.f ? d->eps : 1e-6f;
+  a.status = h->status;
+  cudaError_t e = gemm_launch(a, h->stream);
+  return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);
+}
+
+int hx_attention(hx_handle hh, const hx_attn_desc* d) {
+  hx_ctx* h = H(hh);
+  if (!h || !d) return HX_E_ARG;
+  DevGuard g(h->device);
+  AttnArgs a;
+  a.q = static_cast<const __half*>(d->q);
+  a.ldq = d->ldq;
+  a.q_col0 = d->q_col0;
+  a.k = static_cast<const __half*>(d->k);
+  a.ldk = d->ldk;
+  a.k_col0 = d->k_col0;
+  a.v = static_cast<const __half*>(d->v);
+  a.ldv = d->ldv;
+  a.v_col0 = d->v_col0;
+  a.o = static_cast<__half*>(d->o);
+  a.ldo = d->ldo;
+  a.B = d->batch;
+  a.H = d->heads;
+  a.Tq = d->tq;
+  a.Tk = d->tk;
+  a.nvalid = d->nvalid;
+  a.scale = d->scale;
+  a.status = h->status;
+  cudaError_t e = attn_launch(a, h->stream);
+  return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);
+}
+
+int hx_lnmod(hx_handle hh, const float* x, void* h16, int rows, int D, const float* shift, const float* scale,
+             long vec_bstride, int rows_per_img, float eps) {
+  hx_ctx* h = H(hh);
+  if (!h || !x || !h16 || !shift || !scale) return HX_E_ARG;
+  DevGuard g(h->device);
+  cudaError_t e = lnmod_launch(x, static_cast<__half*>(h16), rows, D, shift, scale, vec_bstride, rows_per_img, eps,
+                               h->stream);
+  return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);
+}
+
+int hx_rmsmod(hx_handle hh, const float* x, void* h16, int rows, int D, const float* w, const float* shift,
+              const float* scale, long vec_bstride, int rows_per_img, float eps) {
+  hx_ctx* h = H(hh);
+  if (!h || !x || !h16 || !shift || !scale) return HX_E_ARG;
+  DevGuard g(h->device);
+  cudaError_t e = rmsmod_launch(x, static_cast<__half*>(h16), rows, D, w, shift, scale, vec_bstride, rows_per_img,
+                                eps, h->stream);
+  return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);
+}
+
+// ---------------------------------------------------------------- rope tables (host)
+int hx_rope_anima(int gh, int gw, double theta, int ntok, float* cs, float* sn) {
+  if (gh <= 0 || gw <= 0 || ntok < gh * gw || !cs || !sn || theta <= 0) return HX_E_ARG;
+  const int dim_h = 128 / 6 * 2, dim_t = 128 - 2 * dim_h, nt = dim_t / 2, nh = dim_h / 2;
+  std::vector<double> fh(nh);
+  for (int i = 0; i < nh; ++i) fh[i] = 1.0 / std::pow(theta, (2.0 * i) / dim_h);
+  std::memset(cs, 0, sizeof(float) * 64 * ntok);
+  std::memset(sn, 0, sizeof(float) * 64 * ntok);
+  for (int tk = 0; tk < gh * gw; ++tk) {
+    const int hh = tk / gw, ww = tk % gw;
+    for (int d = 0; d < 64; ++d) {
+      const double ang = d < nt ? 0.0 : d < nt + nh ? hh * fh[d - nt] : ww * fh[d - nt - nh];
+      cs[tk * 64 + d] = static_cast<float>(std::cos(ang));
+      sn[tk * 64 + d] = static_cast<float>(std::sin(ang));
+    }
+  }
+  return HX_OK;
+}
+
+int hx_rope_moss(int Hh, int Ww, int T, const float* bands, int ntok, float* cs, float* sn) {
+  if (Hh < 0 || Ww < 0 || T < 0 || !bands || !cs || !sn || ntok < Hh * Ww + T) return HX_E_ARG;
+  const int Nimg = Hh * Ww, N = Nimg + T;
+  std::memset(cs, 0, sizeof(float) * 64 * ntok);
+  std::memset(sn, 0, sizeof(float) * 64 * ntok);
+  for (int tk = 0; tk < N; ++tk) {
+    double c[4] = {0, 0, 0, 0};
+    if (tk < Nimg) {
+      c[1] = T;
+      c[2] = tk / Ww - (Hh - 1) / 2.0;
+      c[3] = tk % Ww - (Ww - 1) / 2.0;
+    } else {
+      c[1] = tk - Nimg;
+    }
+    for (int d = 0; d < 64; ++d) {
+      const double a = c[d / 16] * static_cast<double>(bands[d % 16]);
+      cs[tk * 64 + d] = static_cast<float>(std::cos(a));
+      sn[tk * 64 + d] = static_cast<float>(std::sin(a));
+    }
+  }
+  return HX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,184 @@
+// Memory-bound kernels of the block: AdaLN LayerNorm / RMSNorm modulation (fp32 residual in,
+// fp16 operand out), the per-block modulation mat-vecs and small conversions.
+//
+//  lnmod  : k_ln_prep + k_lnmod_s (hexagon/mega/kern.c:31-65): y = (x-mu)*rstd*(1+scale)+shift,
+//           var = E[x^2]-mu^2, no affine, eps 1e-6.
+//  rmsmod : k_rms_prep + k_rmsmod_s (moss/hexagon/mega/kern.c:345-375): y = x*rsqrt(E[x^2]+eps)*w*(1+scale)+shift.
+//  modulation: the helper-thread mat-vecs of megarun (hexagon/mega/megarun.cpp:158-171):
+//           per site h = A[256][D] silu(emb); mod = B[6144][256] h + lora.
+// One warp per row, the row held in registers (D/32 floats per lane), 16-byte loads and stores.
+#include "hx_internal.h"
+#include "hx_ptx.cuh"
+
+namespace hx {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// NV = number of float4 per lane (D = 128 * NV)
+template <int NV, bool RMS>
+__global__ void __launch_bounds__(256) norm_mod_kernel(const float* __restrict__ x, __half* __restrict__ h, int rows,
+                                                       const float* __restrict__ w, const float* __restrict__ shift,
+                                                       const float* __restrict__ scale, long vec_bstride,
+                                                       int rows_per_img, float eps) {
+  constexpr int D = 128 * NV;
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * D);
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] = __ldcs(xr + lane + 32 * i);
+  float s = 0.f, q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    q = fmaf(v[i].x, v[i].x, q);
+    q = fmaf(v[i].y, v[i].y, q);
+    q = fmaf(v[i].z, v[i].z, q);
+    q = fmaf(v[i].w, v[i].w, q);
+  }
+  s = warp_sum(s);
+  q = warp_sum(q);
+  const float inv_d = 1.0f / static_cast<float>(D);
+  float mu = 0.f, rstd;
+  if (RMS) {
+    rstd = rsqrtf(q * inv_d + eps);
+  } else {
+    mu = s * inv_d;
+    rstd = rsqrtf(fmaxf(q * inv_d - mu * mu, 0.f) + eps);
+  }
+  const long voff = static_cast<long>(row / rows_per_img) * vec_bstride;
+  const float4* sh4 = reinterpret_cast<const float4*>(shift + voff);
+  const float4* sc4 = reinterpret_cast<const float4*>(scale + voff);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  uint2* hr = reinterpret_cast<uint2*>(h + static_cast<size_t>(row) * D);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int c = lane + 32 * i;
+    const float4 sh = __ldg(sh4 + c), sc = __ldg(sc4 + c);
+    float4 m = make_float4(1.f + sc.x, 1.f + sc.y, 1.f + sc.z, 1.f + sc.w);
+    if (RMS) {
+      const float4 ww = __ldg(w4 + c);
+      m.x *= ww.x;
+      m.y *= ww.y;
+      m.z *= ww.z;
+      m.w *= ww.w;
+    }
+    const float y0 = fmaf((v[i].x - mu) * rstd, m.x, sh.x), y1 = fmaf((v[i].y - mu) * rstd, m.y, sh.y);
+    const float y2 = fmaf((v[i].z - mu) * rstd, m.z, sh.z), y3 = fmaf((v[i].w - mu) * rstd, m.w, sh.w);
+    hr[c] = make_uint2(pack_half2(y0, y1), pack_half2(y2, y3));
+  }
+}
+
+template <bool RMS>
+cudaError_t norm_dispatch(const float* x, __half* h, int rows, int D, const float* w, const float* shift,
+                          const float* scale, long vec_bstride, int rows_per_img, float eps, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  const int threads = 256, rpb = threads / 32;
+  const int grid = (rows + rpb - 1) / rpb;
+  if (rows_per_img <= 0) rows_per_img = 1 << 30;
+  switch (D) {
+    case 1024: norm_mod_kernel<8, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); break;
+    case 2048: norm_mod_kernel<16, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); break;
+    case 3072: norm_mod_kernel<24, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); break;
+    case 4096: norm_mod_kernel<32, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- modulation mat-vecs
+// stage 1: hid[site][j] = sum_i A[site][j][i] * silu(emb[i]); one warp per (site, j)
+__global__ void mod_stage1(const __half* __restrict__ A, const float* __restrict__ emb, float* __restrict__ hid,
+                           int nsite, int D, int R) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= nsite * R) return;
+  const __half* row = A + static_cast<size_t>(gw) * D;
+  float acc = 0.f;
+  for (int i = lane * 8; i < D; i += 256) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(row + i);
+    const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 wf = __half22float2(w2[t]);
+      const float e0 = emb[i + 2 * t], e1 = emb[i + 2 * t + 1];
+      acc = fmaf(wf.x, e0 / (1.f + expf(-e0)), acc);
+      acc = fmaf(wf.y, e1 / (1.f + expf(-e1)), acc);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) hid[gw] = acc;
+}
+// stage 2: out[site][o] = lora[o] + sum_j B[site][o][j] * hid[site][j]; one warp per (site, o)
+__global__ void mod_stage2(const __half* __restrict__ Bw, const float* __restrict__ hid, const float* __restrict__ lora,
+                           float* __restrict__ out, int nsite, int R, int O) {
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= nsite * O) return;
+  const int site = gw / O, o = gw % O;
+  const __half* row = Bw + static_cast<size_t>(gw) * R;
+  const float* hs = hid + static_cast<size_t>(site) * R;
+  float acc = 0.f;
+  for (int j = lane * 8; j < R; j += 256) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(row + j);
+    const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 wf = __half22float2(w2[t]);
+      acc = fmaf(wf.x, hs[j + 2 * t], acc);
+      acc = fmaf(wf.y, hs[j + 2 * t + 1], acc);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) out[gw] = acc + (lora ? lora[o] : 0.f);
+}
+
+__global__ void f32_to_f16_kernel(const float* __restrict__ s, __half* __restrict__ d, size_t n) {
+  const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const float4 v = *reinterpret_cast<const float4*>(s + i);
+    *reinterpret_cast<uint2*>(d + i) = make_uint2(pack_half2(v.x, v.y), pack_half2(v.z, v.w));
+  } else {
+    for (size_t k = i; k < n; ++k) d[k] = __float2half_rn(s[k]);
+  }
+}
+
+}  // namespace
+
+cudaError_t lnmod_launch(const float* x, __half* h, int rows, int D, const float* shift, const float* scale,
+                         long vec_bstride, int rows_per_img, float eps, cudaStream_t s) {
+  return norm_dispatch<false>(x, h, rows, D, nullptr, shift, scale, vec_bstride, rows_per_img, eps, s);
+}
+
+cudaError_t rmsmod_launch(const float* x, __half* h, int rows, int D, const float* w, const float* shift,
+                          const float* scale, long vec_bstride, int rows_per_img, float eps, cudaStream_t s) {
+  if (!w) return cudaErrorInvalidValue;
+  return norm_dispatch<true>(x, h, rows, D, w, shift, scale, vec_bstride, rows_per_img, eps, s);
+}
+
+// hid scratch lives right after the nsite*O outputs: out must hold nsite*(O+R) floats
+cudaError_t modulation_launch(const __half* Aw, const __half* Bw, const float* emb, const float* lora, float* out,
+                              int nsite, int D, int R, int O, cudaStream_t s) {
+  if (D % 256 || R % 256) return cudaErrorInvalidValue;
+  float* hid = out + static_cast<size_t>(nsite) * O;
+  const int t = 256, wpb = t / 32;
+  mod_stage1<<<(nsite * R + wpb - 1) / wpb, t, 0, s>>>(Aw, emb, hid, nsite, D, R);
+  mod_stage2<<<(nsite * O + wpb - 1) / wpb, t, 0, s>>>(Bw, hid, lora, out, nsite, R, O);
+  return cudaGetLastError();
+}
+
+cudaError_t f32_to_f16_launch(const float* src, __half* dst, size_t n, cudaStream_t s) {
+  if (!n) return cudaSuccess;
+  const size_t threads = 256, per = threads * 4;
+  f32_to_f16_kernel<<<static_cast<unsigned>((n + per - 1) / per), threads, 0, s>>>(src, dst, n);
+  return cudaGetLastError();
+}
+
+}  // namespace hx

@@ -1,0 +1,616 @@
+// Weight-only-quantised GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA.
+//
+// Replaces the reference GEMM engine gemm_run_geo (hexagon/mega/gemm2.c:96-137,
+// moss/hexagon/mega/gemm2.c:145-193): O[M x N] = A[M x K] * W^T with W stored [N][K], weights
+// dequantised while they stream in (dq_tile gemm2.c:20-35, dq4_tile moss gemm2.c:39-56), the
+// LoRA "extra K tiles" of geo.A2 (moss gemm2.h:16) as a second A source, and the flush
+// epilogues of job_fn (gemm2.c:58-82, moss gemm2.c:89-123) fused into the TMEM read-out.
+//
+// Device weight layouts (chosen for this kernel, converted from the pack records at load time):
+//   WF_F16 : fp16 W[N][K]
+//   WF_Q8  : u8   W[N][K], offset binary u = q + 128; fp16 scale[K/g][N]; value = fp16(q * s)
+//   WF_Q4  : u8   W[N][K/2]; every 32-bit word holds 8 consecutive k, k at nibble (k>>1) + 4(k&1);
+//            fp16 scale[K/32][N]; value = fp16((nib - 8) * s)
+//   WF_Q4A : as WF_Q4 plus fp16 min[K/32][N]; value = fp16(fp32(nib * s) + m)   (export_te.py:33-40)
+//
+// CTA = 14 warps, one CTA per SM, persistent over 128x256 output tiles:
+//   warps 0-3  epilogue (TMEM lanes 0-127 = tile rows)
+//   warp  4    TMA producer (A tile, raw weight tile, scales)
+//   warp  5    TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 6-13 dequantisers: raw int8/int4 -> fp16 in the 128B-swizzled K-major operand layout
+// TMEM holds two 128x256 fp32 accumulators so the epilogue of tile i overlaps the mainloop of
+// tile i+1.
+#include <cudaTypedefs.h>
+#include <cstdio>
+#include <mutex>
+
+#include "hx_internal.h"
+#include "hx_ptx.cuh"
+
+namespace hx {
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int EPI_WARPS = 4, TMA_WARP = 4, MMA_WARP = 5, DQ_WARP0 = 6, DQ_WARPS = 8;
+constexpr int GEMM_THREADS = (DQ_WARP0 + DQ_WARPS) * 32;
+constexpr int A_BYTES = BM * BK * 2;      // 16 KB
+constexpr int WDQ_BYTES = BN * BK * 2;    // 32 KB
+constexpr int SC_BYTES = 2048;            // scales (and q4a mins) of one k-block
+
+template <int FMT>
+struct Cfg {
+  static constexpr int RAW_BYTES = FMT == WF_F16 ? 0 : FMT == WF_Q8 ? BN * BK : BN * BK / 2;
+  static constexpr int STAGE_BYTES = A_BYTES + WDQ_BYTES + RAW_BYTES + (FMT == WF_F16 ? 0 : SC_BYTES);
+  static constexpr int STAGES = FMT == WF_F16 ? 4 : 3;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+};
+
+struct KParams {
+  int M, N, nkb, nkb1, group;
+  int num_m_tiles, num_tiles;
+  __half* out;
+  int ldo;
+  float* x;
+  int ldx;
+  const float* gate;
+  long vec_bstride;
+  int rows_per_img;
+  const float* gain0;
+  const float* gain1;
+  int seg1, seg2, rope0, rope1;
+  const float* cosT;
+  const float* sinT;
+  float eps;
+  int* status;
+};
+
+// ---------------------------------------------------------------- dequantisers
+// One k-block (64 k) of a 256-row weight tile: raw smem -> fp16 SW128 K-major smem.
+template <int FMT>
+__device__ __forceinline__ void dequant_kblock(uint32_t raw, uint32_t dq, const __half* sc, int group, int dt) {
+  if constexpr (FMT == WF_Q8) {
+    const int c = dt & 3, r0 = dt >> 2;
+    const __half2 off = __half2half2(__ushort_as_half(0x6480));  // 1152.0
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+      const int n = pass * 64 + r0;
+      const uint4 v = ld_shared_v4(raw + n * 64 + c * 16);
+      const __half s = group == 64 ? sc[n] : sc[(c >> 1) * BN + n];
+      const __half2 s2 = __half2half2(s);
+      uint32_t o[8];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t lo = __byte_perm(w[j], 0x64646464u, 0x4140);
+        uint32_t hi = __byte_perm(w[j], 0x64646464u, 0x4342);
+        __half2 a = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&lo), off), s2);
+        __half2 b = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&hi), off), s2);
+        o[2 * j] = *reinterpret_cast<uint32_t*>(&a);
+        o[2 * j + 1] = *reinterpret_cast<uint32_t*>(&b);
+      }
+      const uint32_t rowb = dq + n * 128, sw = n & 7;
+      st_shared_v4(rowb + (((2 * c) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+      st_shared_v4(rowb + (((2 * c + 1) ^ sw) << 4), o[4], o[5], o[6], o[7]);
+    }
+  } else {
+    // q4 / q4a: 32 raw bytes per row, two threads per row, each thread one 32-k group
+    const int c = dt & 1, r0 = dt >> 1;
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+      const int n = pass * 128 + r0;
+      const uint4 v = ld_shared_v4(raw + n * 32 + c * 16);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      const __half s = sc[c * BN + n];
+      const uint32_t rowb = dq + n * 128, sw = n & 7;
+      if constexpr (FMT == WF_Q4) {
+        const __half2 off = __half2half2(__ushort_as_half(0x6408));  // 1032.0
+        const __half2 s2 = __half2half2(s);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t o[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            uint32_t e = ((w[j] >> (4 * t)) & 0x000F000Fu) | 0x64006400u;
+            __half2 a = __hmul2(__hsub2(*reinterpret_cast<__half2*>(&e), off), s2);
+            o[t] = *reinterpret_cast<uint32_t*>(&a);
+          }
+          st_shared_v4(rowb + (((4 * c + j) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+        }
+      } else {
+        const float sf = __half2float(s);
+        const float mf = __half2float(sc[2 * BN + c * BN + n]);  // mins follow the two scale rows
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t o[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t e = (w[j] >> (4 * t)) & 0x000F000Fu;
+            const float n0 = static_cast<float>(e & 0xF), n1 = static_cast<float>(e >> 16);
+            const float v0 = __fadd_rn(__fmul_rn(n0, sf), mf), v1 = __fadd_rn(__fmul_rn(n1, sf), mf);
+            o[t] = pack_half2(v0, v1);
+          }
+          st_shared_v4(rowb + (((4 * c + j) ^ sw) << 4), o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- epilogue helpers
+__device__ __forceinline__ void store_row32_f16(__half* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    d[q] = make_uint4(pack_half2(v[8 * q], v[8 * q + 1]), pack_half2(v[8 * q + 2], v[8 * q + 3]),
+                      pack_half2(v[8 * q + 4], v[8 * q + 5]), pack_half2(v[8 * q + 6], v[8 * q + 7]));
+}
+
+__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
+__device__ __forceinline__ float situ(float h, float g) {
+  return (4.0f * tanhf(g * 0.25f) * (1.0f / (1.0f + expf(-g)))) * (25.0f * tanhf(h * 0.04f));
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, int m0, int n0, int warp, int lane) {
+  const int m = m0 + warp * 32 + lane;
+  const bool row_ok = m < p.M;
+  const uint32_t tl = tacc + (static_cast<uint32_t>(warp * 32) << 16);
+  const int img = row_ok ? m / p.rows_per_img : 0;
+  uint32_t r[32];
+  float v[32];
+  if constexpr (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_RESID) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int n = n0 + 32 * c;
+      if (n >= p.N) break;  // warp-uniform
+      tmem_ld32(tl + 32 * c, r);
+      tmem_ld_wait();
+      if (!row_ok) continue;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if constexpr (EPI == EPI_RESID) {
+        const float* g = p.gate + img * p.vec_bstride + n;
+        float4* xr = reinterpret_cast<float4*>(p.x + static_cast<size_t>(m) * p.ldx + n);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 gq = *reinterpret_cast<const float4*>(g + 4 * q);
+          float4 xv = xr[q];
+          xv.x += gq.x * v[4 * q];
+          xv.y += gq.y * v[4 * q + 1];
+          xv.z += gq.z * v[4 * q + 2];
+          xv.w += gq.w * v[4 * q + 3];
+          xr[q] = xv;
+        }
+      } else {
+        if constexpr (EPI == EPI_GELU) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+        }
+        store_row32_f16(p.out + static_cast<size_t>(m) * p.ldo + n, v);
+      }
+    }
+  } else if constexpr (EPI == EPI_RMS) {
+#pragma unroll 1
+    for (int hh = 0; hh < BN / 128; ++hh) {
+      const int cb = n0 + 128 * hh;
+      if (cb >= p.N) break;
+      const float* gain = nullptr;
+      int rope = 0;
+      if (cb < p.seg1) {
+        gain = p.gain0;
+        rope = p.rope0;
+      } else if (cb < p.seg2) {
+        gain = p.gain1;
+        rope = p.rope1;
+      }
+      const uint32_t th = tl + 128 * hh;
+      if (gain == nullptr) {  // plain columns (e.g. v)
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(th + 32 * c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          if (row_ok) store_row32_f16(p.out + static_cast<size_t>(m) * p.ldo + cb + 32 * c, v);
+        }
+        continue;
+      }
+      float ss = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(th + 32 * c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float t = __uint_as_float(r[i]);
+          ss = fmaf(t, t, ss);
+        }
+      }
+      const float rs = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
+      __half* orow = p.out + static_cast<size_t>(m) * p.ldo + cb;
+      if (rope) {
+        const int tok = row_ok ? m % p.rows_per_img : 0;
+        const float* cs = p.cosT + static_cast<size_t>(tok) * 64;
+        const float* sn = p.sinT + static_cast<size_t>(tok) * 64;
+        uint32_t r2[32];
+        float lo[32], hi[32];
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld32(th + 32 * c, r);
+          tmem_ld32(th + 64 + 32 * c, r2);
+          tmem_ld_wait();
+          if (!row_ok) continue;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int d = 32 * c + i;
+            const float a = __uint_as_float(r[i]) * rs * gain[d];
+            const float b = __uint_as_float(r2[i]) * rs * gain[d + 64];
+            const float co = cs[d], si = sn[d];
+            lo[i] = a * co - b * si;
+            hi[i] = b * co + a * si;
+          }
+          store_row32_f16(orow + 32 * c, lo);
+          store_row32_f16(orow + 64 + 32 * c, hi);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(th + 32 * c, r);
+          tmem_ld_wait();
+          if (!row_ok) continue;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * rs * gain[32 * c + i];
+          store_row32_f16(orow + 32 * c, v);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_SITU) {
+    // weight rows are interleaved per 256-row tile: [0,128) up_j, [128,256) gate_j of the same outputs
+    uint32_t r2[32];
+    const int o0 = n0 / 2;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      tmem_ld32(tl + 32 * c, r);
+      tmem_ld32(tl + 128 + 32 * c, r2);
+      tmem_ld_wait();
+      if (!row_ok) continue;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = situ(__uint_as_float(r[i]), __uint_as_float(r2[i]));
+      store_row32_f16(p.out + static_cast<size_t>(m) * p.ldo + o0 + 32 * c, v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- the kernel
+template <int FMT, int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
+                const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
+                const __grid_constant__ CUtensorMap tmMin, const KParams p) {
+  using C = Cfg<FMT>;
+  constexpr int S = C::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES);
+  uint64_t* full = bars;            // TMA data landed        (count 1 + tx)
+  uint64_t* dqfull = bars + S;      // dequantised tile ready (count DQ_WARPS)
+  uint64_t* empty = bars + 2 * S;   // MMAs done with stage   (count 1, tcgen05.commit)
+  uint64_t* tfull = bars + 3 * S;   // accumulator ready      (count 1, tcgen05.commit)
+  uint64_t* tempty = tfull + 2;     // accumulator drained    (count EPI_WARPS)
+  uint64_t* drain = tempty + 2;     // abort path: last MMAs complete
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto stage_a = [&](int s) { return smem + s * C::STAGE_BYTES; };
+  auto stage_wdq = [&](int s) { return smem + s * C::STAGE_BYTES + A_BYTES; };
+  auto stage_raw = [&](int s) { return smem + s * C::STAGE_BYTES + A_BYTES + WDQ_BYTES; };
+  auto stage_sc = [&](int s) { return smem + s * C::STAGE_BYTES + A_BYTES + WDQ_BYTES + C::RAW_BYTES; };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&dqfull[i], DQ_WARPS);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tmem_base_slot, 512);
+    tmem_relinquish();
+  }
+  if (warp == TMA_WARP && lane == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmW);
+    if (p.nkb1 < p.nkb) prefetch_tmap(&tmA2);
+    if (FMT != WF_F16) prefetch_tmap(&tmS);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_slot;
+
+  const int ntiles_mine = (p.num_tiles > static_cast<int>(blockIdx.x))
+                              ? (p.num_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                              : 0;
+
+  if (warp == TMA_WARP) {
+    if (lane == 0) {
+      constexpr uint32_t raw_tx = FMT == WF_F16 ? WDQ_BYTES : C::RAW_BYTES;
+      const uint32_t sc_rows = FMT == WF_F16 ? 0 : (BK / p.group);
+      const uint32_t sc_tx = sc_rows * BN * 2 * (FMT == WF_Q4A ? 2 : 1);
+      const uint32_t tx = A_BYTES + raw_tx + sc_tx;
+      int it = 0;
+      bool ok = true;
+      for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
+        const int t = blockIdx.x + ti * gridDim.x;
+        const int m0 = (t % p.num_m_tiles) * BM, n0 = (t / p.num_m_tiles) * BN;
+        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&empty[s], ph ^ 1, p.status, 101)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], tx);
+          if (kb < p.nkb1) tma_load_2d(stage_a(s), &tmA, &full[s], kb * BK, m0);
+          else tma_load_2d(stage_a(s), &tmA2, &full[s], (kb - p.nkb1) * BK, m0);
+          if constexpr (FMT == WF_F16) {
+            tma_load_2d(stage_wdq(s), &tmW, &full[s], kb * BK, n0);
+          } else {
+            tma_load_2d(stage_raw(s), &tmW, &full[s], FMT == WF_Q8 ? kb * BK : kb * (BK / 2), n0);
+            tma_load_2d(stage_sc(s), &tmS, &full[s], n0, kb * static_cast<int>(sc_rows));
+            if constexpr (FMT == WF_Q4A)
+              tma_load_2d(stage_sc(s) + 2 * BN * 2, &tmMin, &full[s], n0, kb * static_cast<int>(sc_rows));
+          }
+        }
+      }
+      if (!ok) {  // drain loads still in flight before the CTA may exit
+        for (int j = (it > S ? it - S : 0); j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == MMA_WARP) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(BM, BN, 0, 0);
+      int it = 0;
+      bool ok = true, issued = false;
+      for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
+        const int acc = ti & 1;
+        if (!mbar_wait(&tempty[acc], ((ti >> 1) & 1) ^ 1, p.status, 102)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t dt = tmem + acc * BN;
+        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&full[s], ph, p.status, 103)) { ok = false; break; }
+          if constexpr (FMT != WF_F16) {
+            if (!mbar_wait(&dqfull[s], ph, p.status, 104)) { ok = false; break; }
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(stage_a(s)), b0 = smem_u32(stage_wdq(s));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            mma_f16_ss(dt, sdesc_sw128(a0 + 32 * k, 16, 1024), sdesc_sw128(b0 + 32 * k, 16, 1024), idesc,
+                       (kb | k) != 0);
+          }
+          issued = true;
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&tfull[acc]);
+      }
+      if (!ok && issued) {
+        mma_commit(drain);
+        mbar_wait(drain, 0, nullptr, 0);
+      }
+    }
+  } else if (warp >= DQ_WARP0) {
+    if constexpr (FMT != WF_F16) {
+      const int dt = threadIdx.x - DQ_WARP0 * 32;
+      int it = 0;
+      bool ok = true;
+      for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
+        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1;
+          if (!mbar_wait(&full[s], ph, p.status, 105)) { ok = false; break; }
+          dequant_kblock<FMT>(smem_u32(stage_raw(s)), smem_u32(stage_wdq(s)),
+                              reinterpret_cast<const __half*>(stage_sc(s)), p.group, dt);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&dqfull[s]);
+        }
+      }
+    }
+  } else {  // epilogue warps 0..3
+    bool ok = true;
+    for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
+      const int t = blockIdx.x + ti * gridDim.x;
+      const int m0 = (t % p.num_m_tiles) * BM, n0 = (t / p.num_m_tiles) * BN;
+      const int acc = ti & 1;
+      if (!mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 106)) { ok = false; break; }
+      tc_fence_after();
+      epilogue_tile<EPI>(p, tmem + acc * BN, m0, n0, warp, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == MMA_WARP) tmem_dealloc(tmem, 512);
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+}  // namespace
+
+// 2D row-major tensor [outer][inner] with row pitch `pitch_bytes`; box [box_outer][box_inner].
+bool make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t inner,
+                  uint64_t outer, uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer,
+                  CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch_bytes & 15) || ((box_inner * esize) & 15)) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, uint64_t d0, uint64_t d1,
+                  uint64_t d2, uint64_t pitch1, uint64_t pitch2, uint32_t b0, uint32_t b1, uint32_t b2,
+                  CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (pitch1 & 15) || (pitch2 & 15) || ((b0 * esize) & 15))
+    return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {pitch1, pitch2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] ? n[dev] : 148;
+}
+
+template <int FMT, int EPI>
+static cudaError_t launch_t(const GemmArgs& a, const KParams& p, const CUtensorMap& tA, const CUtensorMap& tA2,
+                            const CUtensorMap& tW, const CUtensorMap& tS, const CUtensorMap& tMin,
+                            cudaStream_t s) {
+  using C = Cfg<FMT>;
+  static uint64_t attr_set = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1)) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set |= 1ull << dev;
+  }
+  int grid = sm_count();
+  if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
+  if (p.num_tiles < grid) grid = p.num_tiles;
+  gemm_kernel<FMT, EPI><<<grid, GEMM_THREADS, C::SMEM, s>>>(tA, tA2, tW, tS, tMin, p);
+  return cudaGetLastError();
+}
+
+template <int FMT>
+static cudaError_t launch_fmt(const GemmArgs& a, const KParams& p, const CUtensorMap& tA, const CUtensorMap& tA2,
+                              const CUtensorMap& tW, const CUtensorMap& tS, const CUtensorMap& tMin,
+                              cudaStream_t s) {
+  switch (a.epi) {
+    case EPI_STORE: return launch_t<FMT, EPI_STORE>(a, p, tA, tA2, tW, tS, tMin, s);
+    case EPI_RESID: return launch_t<FMT, EPI_RESID>(a, p, tA, tA2, tW, tS, tMin, s);
+    case EPI_GELU: return launch_t<FMT, EPI_GELU>(a, p, tA, tA2, tW, tS, tMin, s);
+    case EPI_RMS: return launch_t<FMT, EPI_RMS>(a, p, tA, tA2, tW, tS, tMin, s);
+    case EPI_SITU: return launch_t<FMT, EPI_SITU>(a, p, tA, tA2, tW, tS, tMin, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
+  const DevMat* W = a.W;
+  if (!W || !a.A || a.M <= 0 || W->N <= 0 || W->K <= 0) return cudaErrorInvalidValue;
+  const int N = W->N, K = W->K;
+  if (K % BK || a.K1 % BK || a.K1 <= 0 || a.K1 > K || N % 32) return cudaErrorInvalidValue;
+  if (a.K1 < K && (!a.A2 || a.lda2 < K - a.K1)) return cudaErrorInvalidValue;
+  if ((a.epi == EPI_RMS || a.epi == EPI_SITU) && N % BN) return cudaErrorInvalidValue;
+  if (a.epi == EPI_RESID && (!a.x || !a.gate)) return cudaErrorInvalidValue;
+  if (a.epi != EPI_RESID && !a.out) return cudaErrorInvalidValue;
+  if (W->fmt == WF_Q8 && W->group != 32 && W->group != 64) return cudaErrorInvalidValue;
+  if ((W->fmt == WF_Q4 || W->fmt == WF_Q4A) && W->group != 32) return cudaErrorInvalidValue;
+
+  CUtensorMap tA, tA2, tW, tS, tMin;
+  memset(&tA2, 0, sizeof tA2);
+  memset(&tS, 0, sizeof tS);
+  memset(&tMin, 0, sizeof tMin);
+  if (!make_tmap_2d(&tA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.A, a.K1, a.M, static_cast<uint64_t>(a.lda) * 2, BK,
+                    BM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (a.K1 < K && !make_tmap_2d(&tA2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.A2, K - a.K1, a.M,
+                                static_cast<uint64_t>(a.lda2) * 2, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  bool ok = true;
+  switch (W->fmt) {
+    case WF_F16:
+      ok = make_tmap_2d(&tW, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, W->w, K, N, static_cast<uint64_t>(K) * 2, BK, BN,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+      break;
+    case WF_Q8:
+      ok = make_tmap_2d(&tW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W->w, K, N, K, BK, BN, CU_TENSOR_MAP_SWIZZLE_NONE);
+      break;
+    default:
+      ok = make_tmap_2d(&tW, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W->w, K / 2, N, K / 2, BK / 2, BN,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  if (ok && W->fmt != WF_F16)
+    ok = make_tmap_2d(&tS, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, W->scale, N, K / W->group,
+                      static_cast<uint64_t>(N) * 2, BN, BK / W->group, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (ok && W->fmt == WF_Q4A)
+    ok = make_tmap_2d(&tMin, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, W->minv, N, K / W->group,
+                      static_cast<uint64_t>(N) * 2, BN, BK / W->group, CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (!ok) return cudaErrorInvalidValue;
+
+  KParams p;
+  p.M = a.M;
+  p.N = N;
+  p.nkb = K / BK;
+  p.nkb1 = a.K1 / BK;
+  p.group = W->fmt == WF_F16 ? 64 : W->group;
+  p.num_m_tiles = (a.M + BM - 1) / BM;
+  p.num_tiles = p.num_m_tiles * ((N + BN - 1) / BN);
+  p.out = a.out;
+  p.ldo = a.ldo;
+  p.x = a.x;
+  p.ldx = a.ldx;
+  p.gate = a.gate;
+  p.vec_bstride = a.vec_bstride;
+  p.rows_per_img = a.rows_per_img > 0 ? a.rows_per_img : (1 << 30);
+  p.gain0 = a.gain0;
+  p.gain1 = a.gain1;
+  p.seg1 = a.seg1;
+  p.seg2 = a.seg2;
+  p.rope0 = a.rope0;
+  p.rope1 = a.rope1;
+  p.cosT = a.cosT;
+  p.sinT = a.sinT;
+  p.eps = a.eps;
+  p.status = a.status;
+  if ((p.rope0 || p.rope1) && (!p.cosT || !p.sinT)) return cudaErrorInvalidValue;
+
+  switch (W->fmt) {
+    case WF_F16: return launch_fmt<WF_F16>(a, p, tA, tA2, tW, tS, tMin, s);
+    case WF_Q8: return launch_fmt<WF_Q8>(a, p, tA, tA2, tW, tS, tMin, s);
+    case WF_Q4: return launch_fmt<WF_Q4>(a, p, tA, tA2, tW, tS, tMin, s);
+    case WF_Q4A: return launch_fmt<WF_Q4A>(a, p, tA, tA2, tW, tS, tMin, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace hx

@@ -1,0 +1,95 @@
+// Internal host-side declarations shared by the kernel files and the C-ABI layer.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+namespace hx {
+
+// Weight storage formats on the device (the layouts are described in gemm.cu).
+enum WFmt : int { WF_F16 = 0, WF_Q8 = 1, WF_Q4A = 2, WF_Q4 = 3 };
+
+// GEMM epilogues. They follow the flush modes of the reference GEMM engine
+// (hexagon/mega/gemm2.c:58-82, moss/hexagon/mega/gemm2.c:89-123).
+enum Epi : int {
+  EPI_STORE = 0,  // out16 = acc
+  EPI_RESID = 1,  // x32 += gate[n] * acc                      (mode 1; mode 4 is the same with full K)
+  EPI_GELU = 2,   // out16 = gelu_erf(acc)                      (mode 2)
+  EPI_RMS = 3,    // per 128-col head: rms * gain (+ rope)      (mode 3)
+  EPI_SITU = 5,   // tile cols [0,128) up, [128,256) gate -> 128 outputs   (mode 5)
+};
+
+// A weight matrix W[N][K] in device memory, in one of the WFmt layouts.
+struct DevMat {
+  int fmt = WF_F16;
+  int N = 0, K = 0;       // output features, reduction length (K includes appended LoRA rows)
+  int group = 32;         // quantisation group along K (q8: 32 or 64; q4/q4a: 32)
+  void* w = nullptr;      // fp16 [N][K] | u8 [N][K] (offset binary) | u8 [N][K/2] (packed nibbles)
+  __half* scale = nullptr;  // [K/group][N]
+  __half* minv = nullptr;   // [K/group][N] (q4a only)
+};
+
+struct GemmArgs {
+  // A: fp16 row-major [M][lda]; columns [0, K1) come from A, [K1, K) from A2 (row-major [M][lda2]).
+  const __half* A = nullptr;
+  int lda = 0;
+  const __half* A2 = nullptr;
+  int lda2 = 0;
+  int M = 0, K1 = 0;
+  const DevMat* W = nullptr;
+  int epi = EPI_STORE;
+  // outputs
+  __half* out = nullptr;  // fp16 [M][ldo]
+  int ldo = 0;
+  float* x = nullptr;     // fp32 residual [M][ldx]
+  int ldx = 0;
+  // per-column vectors; for row m the image is m / rows_per_img and the vector is vec + img * vec_bstride
+  const float* gate = nullptr;
+  long vec_bstride = 0;
+  int rows_per_img = 1 << 30;
+  // EPI_RMS: columns < seg1 use gain0 (rope if rope0), < seg2 gain1 (rope if rope1), others are stored plain
+  const float* gain0 = nullptr;
+  const float* gain1 = nullptr;
+  int seg1 = 0, seg2 = 0, rope0 = 0, rope1 = 0;
+  const float* cosT = nullptr;  // [rows_per_img][64]
+  const float* sinT = nullptr;
+  float eps = 1e-6f;
+  int* status = nullptr;
+  int max_ctas = 0;  // 0 = one CTA per SM
+};
+
+struct AttnArgs {
+  // Q rows [B][Tq][ldq] fp16, head h at column q_col0 + 128 h; likewise K and V.
+  const __half* q = nullptr;
+  int ldq = 0, q_col0 = 0;
+  const __half* k = nullptr;
+  int ldk = 0, k_col0 = 0;
+  const __half* v = nullptr;
+  int ldv = 0, v_col0 = 0;
+  __half* o = nullptr;  // [B][Tq][ldo], head h at column 128 h
+  int ldo = 0;
+  int B = 1, H = 1, Tq = 0, Tk = 0;
+  int nvalid = 0;       // keys with index >= nvalid get probability 0 (0 = all Tk keys valid)
+  float scale = 1.0f;   // logits are q.k * scale
+  int* status = nullptr;
+};
+
+cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s);
+cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s);
+
+// memory-bound kernels (elem.cu)
+cudaError_t lnmod_launch(const float* x, __half* h, int rows, int D, const float* shift, const float* scale,
+                         long vec_bstride, int rows_per_img, float eps, cudaStream_t s);
+cudaError_t rmsmod_launch(const float* x, __half* h, int rows, int D, const float* w, const float* shift,
+                          const float* scale, long vec_bstride, int rows_per_img, float eps, cudaStream_t s);
+cudaError_t modulation_launch(const __half* Aw, const __half* Bw, const float* emb, const float* lora, float* out,
+                              int nsite, int D, int R, int O, cudaStream_t s);
+cudaError_t f32_to_f16_launch(const float* src, __half* dst, size_t n, cudaStream_t s);
+
+// weight repacking from the reference pack records (repack.cu)
+cudaError_t repack_tiles_launch(const uint8_t* rec, int nb, int kb, bool q8, void* dst, __half* scale, int row0,
+                                int nrows_total, int mode, cudaStream_t s);
+int sm_count();
+
+}  // namespace hx

@@ -1,0 +1,245 @@
+/* hxdit.h — C ABI of the B200 DiT block runtime (libhxdit.so).
+ *
+ * Drop-in for the per-block operator the reference drives over FastRPC and the chain runner
+ * around it (Herolias/hexanima):
+ *   mega_open / mega_close         hexagon/mega/mega_imp.c:16-18
+ *   mega_block(meta, wfd, bfd, mod, times, rc)   hexagon/mega/mega.idl:10, hexagon/mega/blk.c:186-197,
+ *                                  moss/hexagon/mega/blk.c:269-281
+ *   rpcmem buffers + fds           hexagon/mega/megarun.cpp:109-127
+ *   per-block modulation thread    hexagon/mega/megarun.cpp:158-171
+ *   chain loop over blocks         hexagon/mega/megarun.cpp:176-184
+ *   gemm_run_geo / attn_run / k_*  hexagon/mega/gemm2.h:16, blk.c:54, kern.h:11-32 (operator level)
+ *
+ * Conventions: plain pointers and sizes, no C++ or torch types. Functions return HX_OK (0) or a
+ * negative HX_E* code; no call aborts the process or traps the GPU. Device pointers ("_dev")
+ * are CUDA device addresses on the handle's device; work is ordered on the handle's stream.
+ * Device kernels bound their waits; a timeout is reported through hx_status / *rc = HX_E_TIMEOUT.
+ */
+#ifndef HXDIT_H
+#define HXDIT_H
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define HX_API __attribute__((visibility("default")))
+#else
+#define HX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status codes
+ * rc values of hx_mega_block follow the reference's (hexagon/mega/blk.c:110-127;
+ * moss/hexagon/mega/blk.c:148-155): 0 ok, negative = failure. */
+#define HX_OK 0
+#define HX_E_ARG (-1)       /* bad argument / handle / size */
+#define HX_E_CUDA (-2)      /* CUDA runtime error (launch, copy, allocation) */
+#define HX_E_NOWEIGHTS (-5) /* unknown weight handle  (reference: -5 weights map failed) */
+#define HX_E_NOBLOB (-6)    /* unknown blob buffer    (reference: -6 no blob) */
+#define HX_E_RANGE (-7)     /* meta offsets reach outside the blob (reference: -7 blob map) */
+#define HX_E_FORMAT (-8)    /* pack bytes do not match a known pack layout */
+#define HX_E_TIMEOUT (-77)  /* a device-side bounded wait expired (reference: -77 HMX self-test) */
+
+/* ------------------------------------------------------------------ models and weight formats */
+#define HX_MODEL_ANIMA 1    /* hexagon/mega: D 2048, 16 heads, self + cross attention, GELU MLP */
+#define HX_MODEL_MOSS 2     /* moss/hexagon/mega: D 3072, 24 heads, joint attention, SiTU MLP, LoRA K tiles */
+
+#define HX_FMT_F16 0        /* fp16 W[N][K] */
+#define HX_FMT_Q8 1         /* u8 W[N][K] offset binary (q+128), fp16 scale[K/group][N], group 32|64 */
+#define HX_FMT_Q4A 2        /* u8 W[N][K/2] nibbles (see hx_mat), fp16 scale and min [K/32][N]: nib*s+m */
+#define HX_FMT_Q4 3         /* as Q4A without min: (nib-8)*s */
+
+typedef struct hx_ctx* hx_handle;
+
+/* ------------------------------------------------------------------ lifecycle
+ * hx_open: mega_open (hexagon/mega/mega_imp.c:16). Binds CUDA device `device`, creates a stream. */
+HX_API int hx_open(int device, hx_handle* out);
+/* hx_close: mega_close (hexagon/mega/mega_imp.c:18). Frees every buffer and weight set of the handle. */
+HX_API int hx_close(hx_handle h);
+/* The CUDA stream (cudaStream_t) the handle launches on; hx_set_stream replaces it (caller-owned). */
+HX_API int hx_get_stream(hx_handle h, void** stream);
+HX_API int hx_set_stream(hx_handle h, void* stream);
+HX_API int hx_sync(hx_handle h);
+/* Device status word written by bounded waits (0 = ok, else the code of the wait that expired);
+ * reading it synchronises the stream and clears it. */
+HX_API int hx_status(hx_handle h, int* status);
+/* Device pointer to the status word, for callers that launch operators on their own streams. */
+HX_API int hx_status_ptr(hx_handle h, int** status_dev);
+
+/* ------------------------------------------------------------------ buffers
+ * Device buffers named by small integer "fds", the analogue of the rpcmem buffers + fds that
+ * megarun maps for the DSP (hexagon/mega/megarun.cpp:109-127). */
+HX_API int hx_buf_alloc(hx_handle h, size_t bytes, int* fd);
+HX_API int hx_buf_free(hx_handle h, int fd);
+HX_API int hx_buf_ptr(hx_handle h, int fd, void** dev);
+HX_API int hx_buf_write(hx_handle h, int fd, size_t off, const void* src, size_t bytes); /* host -> device, stream-ordered, returns when copied */
+HX_API int hx_buf_read(hx_handle h, int fd, size_t off, void* dst, size_t bytes);        /* device -> host, synchronises */
+
+/* ------------------------------------------------------------------ weights */
+typedef struct {
+  int fmt;      /* HX_FMT_* */
+  int n, k;     /* W is [n][k]: n output features, k reduction length (LoRA-B rows included) */
+  int group;    /* quantisation group along k */
+  void* w;      /* fp16 [n][k] | u8 [n][k] | u8 [n][k/2]: in every 32-bit word (8 consecutive k),
+                   k sits at nibble (k>>1) + 4*(k&1) */
+  void* scale;  /* fp16 [k/group][n] */
+  void* minv;   /* fp16 [k/32][n] (Q4A) */
+} hx_mat;
+
+/* matrix slots of hx_weight_desc.mats */
+#define HX_W_QKV 0   /* Anima [3D][D] (q|k|v rows); MOSS [3D][D] when lora == 0 */
+#define HX_W_O 1     /* self-attention output [D][D(+128)] */
+#define HX_W_CQ 2    /* Anima cross-attention q [D][D] */
+#define HX_W_CKV 3   /* Anima cross-attention k|v [2D][Cd] */
+#define HX_W_CO 4    /* Anima cross-attention output [D][D] */
+#define HX_W_M1 5    /* Anima mlp.layer1 [F][D]; MOSS up_gate [2F][D(+128)], rows grouped per 256:
+                        128 up rows then the 128 gate rows of the same outputs */
+#define HX_W_M2 6    /* Anima mlp.layer2 [D][F]; MOSS ffn_down [D][F(+128)] */
+#define HX_W_Q 7     /* MOSS with lora: q, k, v each [D][D+128] */
+#define HX_W_K 8
+#define HX_W_V 9
+#define HX_W_AQKV 10 /* MOSS LoRA down matrices: [384][D], [128][D], [128][D], [128][F] */
+#define HX_W_AO 11
+#define HX_W_AUG 12
+#define HX_W_ADN 13
+#define HX_NMATS 14
+
+typedef struct {
+  int model;         /* HX_MODEL_* */
+  int D, F, Cd, H;   /* hidden size, FFN width, context width (Anima), heads */
+  int lora;          /* MOSS: matrices carry 128 LoRA-B rows at the end of K (export_moss.py:14-27) */
+  hx_mat mats[HX_NMATS];
+  const float* gain; /* device fp32. Anima [512]: q*1/sqrt(128), k, cq*1/sqrt(128), ck (export_all.py:31-32).
+                        MOSS [128+128+D+D]: q/sqrt(128), k, norm1, norm2 (export_moss.py:39) */
+  const void* modA;  /* Anima fp16 [3][256][D]: adaln_modulation_{self_attn,cross_attn,mlp}.1 */
+  const void* modB;  /* Anima fp16 [3][6144][256]: adaln_modulation_*.2 */
+} hx_weight_desc;
+
+/* Load one reference block pack (host bytes of blkNN.bin) into device memory owned by the handle.
+ * Anima: fp16 (W_TOTAL = 138,416,128 B) or q8 (WQ_TOTAL) packs, recognised by size as megarun
+ * does (hexagon/mega/megarun.cpp:97; layout hexagon/mega/blk_wlayout.h:3-20). MOSS: q8 pack of
+ * 135,397,376 B (moss/hexagon/mega/blk_meta.h:6-17). */
+HX_API int hx_weights_load(hx_handle h, int model, const void* pack, size_t bytes, int* wfd);
+/* Bind caller-owned device arrays already in the device layout (no copy; they must outlive use). */
+HX_API int hx_weights_bind(hx_handle h, const hx_weight_desc* desc, int* wfd);
+HX_API int hx_weights_free(hx_handle h, int wfd);
+
+/* ------------------------------------------------------------------ the per-block operator */
+/* Anima meta[] slots: byte offsets into the blob buffer, then scalars.
+ * Same order as hexagon/mega/blk_meta.h:3-5. Weight-offset slots are ignored (weights come from
+ * wfd). Device blob layout (hx_blob_layout fills it):
+ *   X   fp32 [B][NTOK][D] residual stream, updated in place
+ *   CTX fp16 [B][NCTX][Cd]
+ *   MOD fp32 [9][D] (shift, scale, gate per site), read when the call passes mod == NULL
+ *   COS, SIN fp32 [NTOK][64]
+ *   H fp16 [B*NTOK][D]; Q fp16 [B*NTOK][3D] (fused q|k|v; K and V point into it);
+ *   O fp16 [B*NTOK][D]; MID fp16 [B*NTOK][F]; CK fp16 [B*NCTX][2D] (fused ck|cv) */
+enum {
+  HX_A_X = 0, HX_A_CTX, HX_A_MOD, HX_A_GAIN, HX_A_COS, HX_A_SIN,
+  HX_A_WSQ, HX_A_WSK, HX_A_WSV, HX_A_WSO, HX_A_WCQ, HX_A_WCK, HX_A_WCV, HX_A_WCO, HX_A_WM1, HX_A_WM2,
+  HX_A_H, HX_A_Q, HX_A_K, HX_A_V, HX_A_O, HX_A_T, HX_A_MID, HX_A_CK, HX_A_CV,
+  HX_A_NTOK, HX_A_NCTX, HX_A_STOP, HX_A_NW, HX_A_REL, HX_A_FIRST, HX_A_Q8,
+  HX_A_NMETA,               /* 32, the reference's M_NMETA */
+  HX_A_BATCH = HX_A_NMETA,  /* extension: images stacked in the blob (default 1) */
+  HX_A_NMETA_EXT
+};
+/* MOSS meta[] slots (moss/hexagon/mega/blk_meta.h:3-4). Blob layout:
+ *   X fp32 [B][NTOK][D]; COS, SIN fp32 [NTOK][64]; H fp16 [B*NTOK][D]; Q fp16 [B*NTOK][3D] (fused);
+ *   O fp16 [B*NTOK][D]; MID fp16 [B*NTOK][F]; LQ fp16 [B*NTOK][384]; LO, LU, LD fp16 [B*NTOK][128];
+ *   mod: fp32 [6][D] (shift_a, scale_a, gate_a, shift_f, scale_f, gate_f) passed by the call or at CS. */
+enum {
+  HX_S_X = 0, HX_S_COS, HX_S_SIN, HX_S_H, HX_S_Q, HX_S_K, HX_S_V, HX_S_O, HX_S_T, HX_S_MID,
+  HX_S_LQ, HX_S_LO, HX_S_LU, HX_S_LD, HX_S_NTOK, HX_S_NVALID, HX_S_STOP, HX_S_NW, HX_S_REL,
+  HX_S_FIRST, HX_S_MODE, HX_S_NCB, HX_S_FMT, HX_S_ROWS, HX_S_CS, HX_S_WOFF,
+  HX_S_NMETA,               /* 26, the reference's M_NMETA */
+  HX_S_BATCH = HX_S_NMETA,  /* extension: images stacked in the blob (default 1) */
+  HX_S_NMETA_EXT
+};
+
+/* Fill meta[] with a blob layout (megarun.cpp:42-57 layout()) for `batch` images; *total = bytes.
+ * nmeta must be >= HX_A_NMETA_EXT (Anima) or HX_S_NMETA_EXT (MOSS). For MOSS, nctx is unused and
+ * the mod vectors go to the CS slot. */
+HX_API int hx_blob_layout(int model, int ntok, int nctx, int batch, int D, int F, int Cd, int32_t* meta, int nmeta,
+                   size_t* total);
+
+/* One DiT block forward: mega_block (hexagon/mega/mega.idl:10). mod: host fp32 modulation
+ * (Anima 9*D floats, MOSS 6*D; modlen in bytes) copied per call, or NULL to read it from the blob.
+ * times[0..]: per-stage microseconds when ntimes > 0 (synchronises; slot order of the reference's
+ * TICKs, times[24] = entry latency). *rc: HX_OK or a negative HX_E* code. */
+HX_API int hx_mega_block(hx_handle h, const int32_t* meta, int nmeta, int wfd, int bfd, const uint8_t* mod, int modlen,
+                  int32_t* times, int ntimes, int32_t* rc);
+
+/* Per-block AdaLN modulation of an Anima block (megarun.cpp:158-171):
+ * for site s: mod[3s..3s+2][D] = B_s (A_s silu(emb)) + lora[0:3D]. emb [D], lora [3D], mod [9D]
+ * device fp32; mod_dev must hold 9*D + 3*256 floats (the tail is scratch). */
+HX_API int hx_modulation(hx_handle h, int wfd, const float* emb_dev, const float* lora_dev, float* mod_dev);
+
+/* Run `count` blocks in order on one blob: the megarun chain (megarun.cpp:176-184).
+ * Anima: mods_dev NULL -> each block's modulation is computed from emb_dev/lora_dev first;
+ * otherwise mods_dev holds count*9*D floats. skipmask bit k skips block k (x passes through).
+ * use_graph != 0 captures the chain once in a CUDA graph and replays it while the arguments repeat. */
+HX_API int hx_chain(hx_handle h, const int32_t* meta, int nmeta, const int* wfds, int count, int bfd,
+             const float* mods_dev, const float* emb_dev, const float* lora_dev, uint32_t skipmask, int use_graph,
+             int32_t* rc);
+
+/* ------------------------------------------------------------------ operator level (device pointers) */
+typedef struct {
+  const void* a; int lda;       /* fp16 [m][lda], columns [0,k1) */
+  const void* a2; int lda2;     /* fp16 [m][lda2]: columns [k1, w.k) (LoRA extra K tiles, gemm_geo_t.A2) */
+  int m, k1;
+  hx_mat w;
+  int epi;                      /* HX_EPI_* */
+  void* out; int ldo;           /* fp16 output */
+  float* x; int ldx;            /* fp32 residual (HX_EPI_RESID) */
+  const float* gate;            /* [n] (+ image * vec_bstride) */
+  long vec_bstride; int rows_per_img;
+  const float* gain0; const float* gain1;   /* HX_EPI_RMS: per-head gains [128] */
+  int seg1, seg2, rope0, rope1;
+  const float* cos_t; const float* sin_t;   /* [rows_per_img][64] */
+  float eps;
+} hx_gemm_desc;
+#define HX_EPI_STORE 0
+#define HX_EPI_RESID 1
+#define HX_EPI_GELU 2
+#define HX_EPI_RMS 3
+#define HX_EPI_SITU 5
+/* O = A W^T with a fused epilogue: gemm_run_geo (hexagon/mega/gemm2.c:96-137, moss gemm2.c:145-193). */
+HX_API int hx_gemm(hx_handle h, const hx_gemm_desc* d);
+
+typedef struct {
+  const void* q; int ldq, q_col0;
+  const void* k; int ldk, k_col0;
+  const void* v; int ldv, v_col0;
+  void* o; int ldo;
+  int batch, heads, tq, tk, nvalid;
+  float scale;
+} hx_attn_desc;
+/* softmax(q k^T * scale) v per head, head_dim 128: attn_run (hexagon/mega/blk.c:54-91,
+ * masked moss/hexagon/mega/blk.c:54-94). Keys >= nvalid are masked (0 = none). */
+HX_API int hx_attention(hx_handle h, const hx_attn_desc* d);
+
+/* k_lnmod_s (hexagon/mega/kern.c:31-65): h16 = LN(x) * (1 + scale) + shift, eps 1e-6 by convention. */
+HX_API int hx_lnmod(hx_handle h, const float* x, void* h16, int rows, int D, const float* shift, const float* scale,
+             long vec_bstride, int rows_per_img, float eps);
+/* k_rmsmod_s (moss/hexagon/mega/kern.c:345-375): h16 = x rsqrt(mean x^2 + eps) w (1 + scale) + shift. */
+HX_API int hx_rmsmod(hx_handle h, const float* x, void* h16, int rows, int D, const float* w, const float* shift,
+              const float* scale, long vec_bstride, int rows_per_img, float eps);
+
+/* Host-side RoPE tables [ntok][64] (angle index d of the 64 split-half pairs (d, d+64)).
+ * Anima 3D split t/h/w = 22/21/21 angles, theta for h and w (make_rope, hexagon/mega/megarun.cpp:77-90);
+ * theta 10000 reproduces megarun. Rows >= gh*gw are zero. */
+HX_API int hx_rope_anima(int gh, int gw, double theta, int ntok, float* cos_out, float* sin_out);
+/* MOSS 4D rope (rope_tables, moss/mossrun/mossrun.cpp:190-202; moss/moss_ref.py:27-35):
+ * image token (y, x): coords (0, T, y-(H-1)/2, x-(W-1)/2); text token i: (0, i, 0, 0);
+ * angle d = coord[d/16] * bands[d%16]. Rows >= H*W + T are zero. */
+HX_API int hx_rope_moss(int H, int W, int T, const float* bands16, int ntok, float* cos_out, float* sin_out);
+
+/* Library version string. */
+HX_API const char* hx_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HXDIT_H */

@@ -1,0 +1,167 @@
+"""Anima DiT block oracle in torch fp32 — test infrastructure, see oracle/__init__.py.
+
+Restates hexagon/mega/blk.c:148-175 (the reference ships no runnable Anima block in Python):
+  site 0: h = LNmod(x); q, k, v = h W; q, k = RoPE(RMS(q|k) * gain); o = attn(q, k, v); x += gate * o Wo
+  site 1: h = LNmod(x); q = RMS(h Wcq) * gain; ck = RMS(ctx Wck) * gain; cv = ctx Wcv;
+          o = attn(q, ck, cv) over all context rows (zero-padded rows are NOT masked, PITFALLS:71);
+          x += gate * o Wco
+  site 2: h = LNmod(x); x += gate * GELU(h Wm1) Wm2
+with
+  LNmod   kern.c:38-65   y = (x - mu) / sqrt(E[x^2] - mu^2 + 1e-6) * (1 + scale) + shift (no affine)
+  RMS     kern.c:199-232 per 128-wide head: x / sqrt(mean x^2 + 1e-6) * gain
+  RoPE    kern.c:213-222 split-half pairs (d, d+64): lo = a c - b s, hi = b c + a s
+  gains   export_all.py:31-32  [q/sqrt(128), k, cq/sqrt(128), ck]; attention scale 1.0
+  GELU    ktest.c:63     exact erf form
+  tables  megarun.cpp:77-90   angles d<22: 0; d<43: row * th^(-2i/42); else col * th^(-2i/42)
+  mod     megarun.cpp:158-171 per site: B (A silu(emb)) + lora; chunks shift, scale, gate
+Weights are [out][in] (torch Linear layout); the pack stores their transposes as W[K][N] tiles.
+"""
+import math
+
+import numpy as np
+import torch
+
+HD = 128
+ORDER = ["sq", "sk", "sv", "so", "cq", "ck", "cv", "co", "m1", "m2"]  # export_all.py:9 order
+
+
+def ln_mod(x, shift, scale, eps=1e-6):
+    mu = x.mean(-1, keepdim=True)
+    var = (x * x).mean(-1, keepdim=True) - mu * mu
+    return (x - mu) * torch.rsqrt(var.clamp_min(0) + eps) * (1 + scale) + shift
+
+
+def rms_head(x, gain, eps=1e-6):
+    """x [..., H, 128]"""
+    return x * torch.rsqrt(x.square().mean(-1, keepdim=True) + eps) * gain
+
+
+def rope(x, cos, sin):
+    """x [B, T, H, 128]; cos, sin [T, 64]"""
+    a, b = x[..., :64], x[..., 64:]
+    c, s = cos[None, :, None, :], sin[None, :, None, :]
+    return torch.cat((a * c - b * s, b * c + a * s), -1)
+
+
+def attention(q, k, v, scale=1.0, nvalid=None):
+    """q [B, Tq, H, d], k, v [B, Tk, H, d] -> [B, Tq, H, d]; keys >= nvalid masked."""
+    s = torch.einsum("bqhd,bkhd->bhqk", q, k) * scale
+    if nvalid is not None and nvalid < k.shape[1]:
+        s[..., nvalid:] = float("-inf")
+    p = torch.softmax(s, -1)
+    return torch.einsum("bhqk,bkhd->bqhd", p, v)
+
+
+def gelu(x):
+    return 0.5 * x * (1 + torch.erf(x / math.sqrt(2.0)))
+
+
+def make_rope(gh, gw, theta=10000.0, ntok=None):
+    """cos, sin float32 [ntok][64]."""
+    ntok = ntok or gh * gw
+    dim_h = 128 // 6 * 2
+    nt, nh = (128 - 2 * dim_h) // 2, dim_h // 2
+    fh = 1.0 / np.power(float(theta), 2.0 * np.arange(nh) / dim_h)
+    tk = np.arange(gh * gw)
+    hh, ww = tk // gw, tk % gw
+    ang = np.zeros((gh * gw, 64))
+    ang[:, nt:nt + nh] = hh[:, None] * fh[None, :]
+    ang[:, nt + nh:] = ww[:, None] * fh[None, :]
+    cos = np.zeros((ntok, 64), np.float32)
+    sin = np.zeros((ntok, 64), np.float32)
+    cos[: gh * gw] = np.cos(ang)
+    sin[: gh * gw] = np.sin(ang)
+    return cos, sin
+
+
+def modulation(modA, modB, emb, lora):
+    """modA [3][256][D], modB [3][3D][256] (fp16 values), emb [D], lora [3D] -> mod [9][D] fp32."""
+    s = emb * torch.sigmoid(emb)
+    out = []
+    for site in range(3):
+        h1 = modA[site].float() @ s
+        out.append(modB[site].float() @ h1 + lora)
+    D = emb.shape[0]
+    return torch.cat(out).view(9, D)
+
+
+def block(x, ctx, mod, cos, sin, W, gain, heads=None):
+    """x [B, T, D] fp32, ctx [B, C, Cd], mod [9][D], cos/sin [T][64], W[name] [out][in], gain [512] -> new x."""
+    B, T, D = x.shape
+    H = heads or D // HD
+    x = x.clone()
+    lin = lambda a, n: a @ W[n].T
+    for site in range(3):
+        sh, sc, gt = mod[3 * site], mod[3 * site + 1], mod[3 * site + 2]
+        h = ln_mod(x, sh, sc)
+        if site == 0:
+            q = rope(rms_head(lin(h, "sq").view(B, T, H, HD), gain[0:128]), cos, sin)
+            k = rope(rms_head(lin(h, "sk").view(B, T, H, HD), gain[128:256]), cos, sin)
+            v = lin(h, "sv").view(B, T, H, HD)
+            o = attention(q, k, v).reshape(B, T, D)
+            x = x + gt * lin(o, "so")
+        elif site == 1:
+            C = ctx.shape[1]
+            q = rms_head(lin(h, "cq").view(B, T, H, HD), gain[256:384])
+            ck = rms_head(lin(ctx, "ck").view(B, C, H, HD), gain[384:512])
+            cv = lin(ctx, "cv").view(B, C, H, HD)
+            o = attention(q, ck, cv).reshape(B, T, D)
+            x = x + gt * lin(o, "co")
+        else:
+            x = x + gt * lin(gelu(lin(h, "m1")), "m2")
+    return x
+
+
+def init_weights(seed, D=2048, F=8192, Cd=1024, std=0.02):
+    """Seeded synthetic block: weights ~N(0, std), norm gains 1 + N(0, std), mod weights ~N(0, std)."""
+    g = torch.Generator().manual_seed(seed)
+    n = lambda *s: torch.randn(*s, generator=g) * std
+    W = {"sq": n(D, D), "sk": n(D, D), "sv": n(D, D), "so": n(D, D), "cq": n(D, D), "ck": n(D, Cd), "cv": n(D, Cd),
+         "co": n(D, D), "m1": n(F, D), "m2": n(D, F)}
+    norms = {k: 1 + n(HD) for k in ("q", "k", "cq", "ck")}
+    modA = n(3, 256, D).half()
+    modB = n(3, 3 * D, 256).half()
+    return W, norms, modA, modB
+
+
+def pack_gain(norms):
+    """[q/sqrt(128), k, cq/sqrt(128), ck] fp32 (export_all.py:31-32)."""
+    sc = 1.0 / math.sqrt(HD)
+    return torch.cat([norms["q"] * sc, norms["k"], norms["cq"] * sc, norms["ck"]]).float()
+
+
+def build_pack(W, norms, modA, modB, q8=False):
+    """blkNN.bin bytes (export_all.py main loop): 10 matrices as tiles of W^T, gains padded to 4096 B, mod weights."""
+    from .packs import F16_FLOOR_ANIMA, q8tiles, wt16
+    parts = []
+    for name in ORDER:
+        t = wt16(W[name].T.contiguous().numpy())
+        parts.append(q8tiles(t, F16_FLOOR_ANIMA) if q8 else t.tobytes())
+    g = pack_gain(norms).numpy().astype(np.float32)
+    parts.append(g.tobytes() + bytes(4096 - g.nbytes))
+    for site in range(3):
+        parts.append(modA[site].numpy().astype(np.float16).tobytes())
+        parts.append(modB[site].numpy().astype(np.float16).tobytes())
+    return b"".join(parts)
+
+
+def pack_weights(pack, D=2048, F=8192, Cd=1024, q8=False):
+    """The fp32 [out][in] weights the device multiplies after loading `pack` (fp16 values or fp16(q*s))."""
+    from .packs import dequant_q8_f16, unwt16
+    dims = {"sq": (D, D), "sk": (D, D), "sv": (D, D), "so": (D, D), "cq": (D, D), "ck": (Cd, D), "cv": (Cd, D),
+            "co": (D, D), "m1": (D, F), "m2": (F, D)}  # (K, N)
+    W, off = {}, 0
+    for name in ORDER:
+        K, N = dims[name]
+        nb, kb = N // 32, K // 32
+        if q8:
+            size = nb * kb * 1152
+            w = dequant_q8_f16(pack[off:off + size], nb, kb)
+        else:
+            size = nb * kb * 2048
+            t = np.frombuffer(pack[off:off + size], np.float16).reshape(nb, kb, 16, 32, 2)
+            w = unwt16(t)
+        W[name] = torch.from_numpy(w.astype(np.float32).T.copy())
+        off += size
+    gain = torch.from_numpy(np.frombuffer(pack[off:off + 2048], np.float32).copy())
+    return W, gain

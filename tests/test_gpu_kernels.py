@@ -1,0 +1,184 @@
+"""Kernel-level parity on the GPU, through the C ABI (hx_gemm / hx_attention / hx_lnmod / hx_rmsmod).
+
+Tolerances: dequantisation bit-exact; GEMM / attention outputs within fp16-output rounding of an
+fp32 reference computed from the same fp16 operands (rel-L2 <= 2e-3 per output tensor)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from hexanima_b200 import runtime as rt
+from oracle import anima as oa
+from oracle import moss as om
+from tests.gpu_util import make_mat, rel
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def h():
+    hd = rt.Handle(0)
+    yield hd
+    assert hd.status() == 0
+    hd.close()
+
+
+def _onehot_dequant(h, fmt, w, group):
+    """out = I * W^T reproduces the device's dequantised operand exactly (one fp32 product per output)."""
+    N, K = w.shape
+    mat, keep, deq = make_mat(fmt, w, group)
+    A = torch.eye(K, dtype=torch.float16, device="cuda")
+    out = torch.zeros(K, N, dtype=torch.float16, device="cuda")
+    h.gemm(A, K, mat, rt.EPI_STORE, lda=K, out=out, ldo=N)
+    h.sync()
+    return out.cpu().T.contiguous(), deq
+
+
+@pytest.mark.parametrize("fmt,group", [(rt.FMT_F16, 64), (rt.FMT_Q8, 32), (rt.FMT_Q8, 64), (rt.FMT_Q4, 32),
+                                       (rt.FMT_Q4A, 32)])
+def test_dequant_bit_exact(h, fmt, group):
+    rng = np.random.default_rng(7)
+    N, K = 320, 256
+    w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+    w[3] *= 1e-3     # small scales: subnormal fp16 products
+    w[7] *= 300.0    # large values
+    w[11] = 0.0
+    got, deq = _onehot_dequant(h, fmt, w, group)
+    ref = deq.half()
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), int((got != ref).sum())
+
+
+def _ref_gemm(A16, Wd):
+    return A16.float().cpu() @ Wd.T
+
+
+@pytest.mark.parametrize("fmt", [rt.FMT_F16, rt.FMT_Q8, rt.FMT_Q4])
+def test_gemm_store_and_gelu(h, fmt):
+    torch.manual_seed(1)
+    M, K, N = 300, 512, 544
+    A = torch.randn(M, K).half()
+    mat, keep, Wd = make_mat(fmt, (torch.randn(N, K) * 0.05).numpy(), 32)
+    ref = _ref_gemm(A, Wd)
+    for epi, f in ((rt.EPI_STORE, lambda t: t), (rt.EPI_GELU, oa.gelu)):
+        out = torch.zeros(M, N, dtype=torch.float16, device="cuda")
+        h.gemm(A.cuda(), M, mat, epi, lda=K, out=out, ldo=N)
+        h.sync()
+        assert rel(out.float(), f(ref)) < 2e-3
+
+
+def test_gemm_large_k_and_lora_a2(h):
+    torch.manual_seed(2)
+    M, K1, N = 256, 8192, 512
+    A = torch.randn(M, K1).half() * 0.5
+    L = torch.randn(M, 384).half()
+    W = torch.randn(N, K1 + 128) * 0.02
+    mat, keep, Wd = make_mat(rt.FMT_Q8, W.numpy(), 32)
+    out = torch.zeros(M, N, dtype=torch.float16, device="cuda")
+    Lc = L.cuda()
+    # extra K columns come from columns 128..255 of L (the k slice of the fused LoRA-A output)
+    h.gemm(A.cuda(), M, mat, rt.EPI_STORE, lda=K1, k1=K1, a2=Lc.data_ptr() + 128 * 2, lda2=384, out=out, ldo=N)
+    h.sync()
+    ref = torch.cat((A.float(), L[:, 128:256].float()), 1) @ Wd.T
+    assert rel(out.float(), ref) < 2e-3
+
+
+def test_gemm_residual(h):
+    torch.manual_seed(3)
+    B, T, K, N = 2, 160, 256, 512
+    M = B * T
+    A = torch.randn(M, K).half()
+    mat, keep, Wd = make_mat(rt.FMT_Q8, (torch.randn(N, K) * 0.05).numpy(), 64)
+    x0 = torch.randn(M, N)
+    gate = torch.randn(B, N)
+    x = x0.cuda()
+    g = gate.cuda()
+    h.gemm(A.cuda(), M, mat, rt.EPI_RESID, lda=K, x=x, ldx=N, gate=g, vec_bstride=N, rows_per_img=T)
+    h.sync()
+    ref = x0 + gate.repeat_interleave(T, 0) * _ref_gemm(A, Wd)
+    assert rel(x.cpu() - x0, ref - x0) < 2e-3
+
+
+def test_gemm_rms_rope_segments(h):
+    torch.manual_seed(4)
+    T, K, D = 192, 256, 256  # 2 heads per segment; q | k | v = 768 columns
+    A = torch.randn(T, K).half()
+    mat, keep, Wd = make_mat(rt.FMT_F16, (torch.randn(3 * D, K) * 0.05).numpy())
+    gq, gk = 1 + 0.1 * torch.randn(128), 1 + 0.1 * torch.randn(128)
+    ang = torch.rand(T, 64) * 6.0
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    out = torch.zeros(T, 3 * D, dtype=torch.float16, device="cuda")
+    gqc, gkc, cc, sc = gq.cuda(), gk.cuda(), cos.cuda(), sin.cuda()
+    h.gemm(A.cuda(), T, mat, rt.EPI_RMS, lda=K, out=out, ldo=3 * D, gain0=gqc, gain1=gkc, seg1=D, seg2=2 * D,
+           rope0=1, rope1=1, cos_t=cc, sin_t=sc, rows_per_img=T)
+    h.sync()
+    ref = _ref_gemm(A, Wd)
+    H = D // 128
+    q = oa.rope(oa.rms_head(ref[:, :D].view(1, T, H, 128), gq), cos, sin).reshape(T, D)
+    k = oa.rope(oa.rms_head(ref[:, D:2 * D].view(1, T, H, 128), gk), cos, sin).reshape(T, D)
+    o = out.float().cpu()
+    assert rel(o[:, :D], q) < 2e-3 and rel(o[:, D:2 * D], k) < 2e-3 and rel(o[:, 2 * D:], ref[:, 2 * D:]) < 2e-3
+
+
+def test_gemm_situ(h):
+    torch.manual_seed(5)
+    M, K, F = 200, 256, 512
+    A = torch.randn(M, K).half()
+    up, gate = torch.randn(F, K) * 0.1, torch.randn(F, K) * 0.1
+    from oracle import packs as op
+    w = op.situ_rows(up.numpy(), gate.numpy())
+    mat, keep, Wd = make_mat(rt.FMT_Q8, w, 32)
+    out = torch.zeros(M, F, dtype=torch.float16, device="cuda")
+    h.gemm(A.cuda(), M, mat, rt.EPI_SITU, lda=K, out=out, ldo=F)
+    h.sync()
+    ug = _ref_gemm(A, Wd).view(M, F // 128, 2, 128)
+    ref = om.situ(ug[:, :, 0], ug[:, :, 1]).reshape(M, F)
+    assert rel(out.float(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("B,H,Tq,Tk,nvalid", [(2, 2, 200, 333, 300), (1, 3, 256, 256, 0), (2, 16, 1536, 1536, 0),
+                                               (1, 2, 130, 70, 0)])
+def test_attention(h, B, H, Tq, Tk, nvalid):
+    torch.manual_seed(6)
+    D = 128 * H
+    # q lives in a fused [q | k | v] row buffer, k and v in a separate one, exercising column offsets
+    qbuf = (torch.randn(B, Tq, 3 * D) * 0.6).half()
+    kv = (torch.randn(B, Tk, 2 * D) * 0.6).half()
+    out = torch.zeros(B, Tq, D, dtype=torch.float16, device="cuda")
+    scale = 1.0 / math.sqrt(128)
+    qc, kvc = qbuf.cuda(), kv.cuda()
+    h.attention(qc, kvc, kvc, out, B, H, Tq, Tk, 3 * D, 2 * D, 2 * D, D, q_col0=D, k_col0=0, v_col0=D,
+                nvalid=nvalid, scale=scale)
+    h.sync()
+    q = qbuf[..., D:2 * D].float().view(B, Tq, H, 128)
+    k = kv[..., :D].float().view(B, Tk, H, 128)
+    v = kv[..., D:].float().view(B, Tk, H, 128)
+    ref = oa.attention(q, k, v, scale=scale, nvalid=nvalid or None).reshape(B, Tq, D)
+    assert rel(out.float(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("D", [1024, 2048, 3072])
+def test_lnmod_rmsmod(h, D):
+    torch.manual_seed(8)
+    B, T = 2, 96
+    x = torch.randn(B * T, D) * 3 + 0.5
+    sh, sc, w = torch.randn(B, D) * 0.1, torch.randn(B, D) * 0.1, 1 + torch.randn(D) * 0.1
+    out = torch.zeros(B * T, D, dtype=torch.float16, device="cuda")
+    h.lnmod(x.cuda(), out, B * T, D, sh.cuda(), sc.cuda(), vec_bstride=D, rows_per_img=T)
+    h.sync()
+    ref = oa.ln_mod(x.view(B, T, D), sh[:, None], sc[:, None]).reshape(B * T, D)
+    assert rel(out.float(), ref) < 1e-3
+    h.rmsmod(x.cuda(), out, B * T, D, w.cuda(), sh.cuda(), sc.cuda(), vec_bstride=D, rows_per_img=T)
+    h.sync()
+    ref = (om.rms(x.view(B, T, D), w) * (1 + sc[:, None]) + sh[:, None]).reshape(B * T, D)
+    assert rel(out.float(), ref) < 1e-3
+
+
+def test_bad_arguments_are_rejected(h):
+    mat, keep, _ = make_mat(rt.FMT_F16, np.zeros((64, 100), np.float32))  # K not a multiple of 64
+    A = torch.zeros(64, 100, dtype=torch.float16, device="cuda")
+    out = torch.zeros(64, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(rt.HxError):
+        h.gemm(A, 64, mat, rt.EPI_STORE, lda=100, out=out, ldo=64)
+    with pytest.raises(rt.HxError):
+        h.attention(A, A, A, out, 1, 1, 64, 64, 100, 100, 100, 64)  # row pitch not 16-byte aligned
