@@ -83,13 +83,16 @@ cudaError_t norm_dispatch(const float* x, __half* h, int rows, int D, const floa
   const int threads = 256, rpb = threads / 32;
   const int grid = (rows + rpb - 1) / rpb;
   if (rows_per_img <= 0) rows_per_img = 1 << 30;
+#define HX_NORM_CASE(NV)                                                                                   \
+  case 128 * NV:                                                                                            \
+    norm_mod_kernel<NV, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); \
+    break;
   switch (D) {
-    case 1024: norm_mod_kernel<8, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); break;
-    case 2048: norm_mod_kernel<16, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); break;
-    case 3072: norm_mod_kernel<24, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); break;
-    case 4096: norm_mod_kernel<32, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); break;
+    HX_NORM_CASE(1) HX_NORM_CASE(2) HX_NORM_CASE(3) HX_NORM_CASE(4) HX_NORM_CASE(6) HX_NORM_CASE(8)
+    HX_NORM_CASE(12) HX_NORM_CASE(16) HX_NORM_CASE(24) HX_NORM_CASE(32)
     default: return cudaErrorInvalidValue;
   }
+#undef HX_NORM_CASE
   return cudaGetLastError();
 }
 

@@ -43,7 +43,8 @@ struct Cfg {
   static constexpr int RAW_BYTES = FMT == WF_F16 ? 0 : FMT == WF_Q8 ? BN * BK : BN * BK / 2;
   static constexpr int STAGE_BYTES = A_BYTES + WDQ_BYTES + RAW_BYTES + (FMT == WF_F16 ? 0 : SC_BYTES);
   static constexpr int STAGES = FMT == WF_F16 ? 4 : 3;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+  static constexpr int OUT_STAGE = 16384;  // residual epilogue: 128 rows x 32 fp32, 128B-swizzled
+  static constexpr int SMEM = STAGES * STAGE_BYTES + OUT_STAGE + 1024 /*barriers*/ + 1024 /*alignment slack*/;
 };
 
 struct KParams {
@@ -152,11 +153,15 @@ __device__ __forceinline__ float situ(float h, float g) {
 }
 
 template <int EPI>
-__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, int m0, int n0, int warp, int lane) {
+__device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, int m0, int n0, int warp, int lane,
+                                              const CUtensorMap* tmX, uint8_t* stage_ptr) {
   const int m = m0 + warp * 32 + lane;
   const bool row_ok = m < p.M;
   const uint32_t tl = tacc + (static_cast<uint32_t>(warp * 32) << 16);
   const int img = row_ok ? m / p.rows_per_img : 0;
+  const uint32_t stage = smem_u32(stage_ptr);
+  (void)stage;
+  (void)tmX;
   uint32_t r[32];
   float v[32];
   if constexpr (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_RESID) {
@@ -166,21 +171,28 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
       if (n >= p.N) break;  // warp-uniform
       tmem_ld32(tl + 32 * c, r);
       tmem_ld_wait();
-      if (!row_ok) continue;
+      if (EPI != EPI_RESID && !row_ok) continue;
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
       if constexpr (EPI == EPI_RESID) {
+        // x += gate * acc: stage gate*acc in shared memory and let TMA add it into x in L2
+        // (no read of x by the SM). Chunk c of the previous iteration must have left the buffer.
         const float* g = p.gate + img * p.vec_bstride + n;
-        float4* xr = reinterpret_cast<float4*>(p.x + static_cast<size_t>(m) * p.ldx + n);
+        const int row = warp * 32 + lane;
+        if (threadIdx.x == 0) bulk_wait_read<0>();
+        named_bar(1, EPI_WARPS * 32);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const float4 gq = *reinterpret_cast<const float4*>(g + 4 * q);
-          float4 xv = xr[q];
-          xv.x += gq.x * v[4 * q];
-          xv.y += gq.y * v[4 * q + 1];
-          xv.z += gq.z * v[4 * q + 2];
-          xv.w += gq.w * v[4 * q + 3];
-          xr[q] = xv;
+          const uint32_t addr = stage + row * 128 + ((q ^ (row & 7)) << 4);
+          st_shared_v4(addr, __float_as_uint(gq.x * v[4 * q]), __float_as_uint(gq.y * v[4 * q + 1]),
+                       __float_as_uint(gq.z * v[4 * q + 2]), __float_as_uint(gq.w * v[4 * q + 3]));
+        }
+        fence_proxy_async_smem();
+        named_bar(1, EPI_WARPS * 32);
+        if (threadIdx.x == 0) {
+          tma_reduce_add_2d(tmX, stage_ptr, n, m0);
+          bulk_commit();
         }
       } else {
         if constexpr (EPI == EPI_GELU) {
@@ -233,25 +245,41 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
         const int tok = row_ok ? m % p.rows_per_img : 0;
         const float* cs = p.cosT + static_cast<size_t>(tok) * 64;
         const float* sn = p.sinT + static_cast<size_t>(tok) * 64;
-        uint32_t r2[32];
-        float lo[32], hi[32];
+        uint32_t a16[16], b16[16];
 #pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(th + 32 * c, r);
-          tmem_ld32(th + 64 + 32 * c, r2);
+        for (int c = 0; c < 4; ++c) {  // pairs (d, d+64), 16 angles at a time
+          tmem_ld16(th + 16 * c, a16);
+          tmem_ld16(th + 64 + 16 * c, b16);
           tmem_ld_wait();
           if (!row_ok) continue;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int d = 32 * c + i;
-            const float a = __uint_as_float(r[i]) * rs * gain[d];
-            const float b = __uint_as_float(r2[i]) * rs * gain[d + 64];
-            const float co = cs[d], si = sn[d];
-            lo[i] = a * co - b * si;
-            hi[i] = b * co + a * si;
+          for (int i = 0; i < 16; i += 4) {
+            const int d = 16 * c + i;
+            const float4 ga = *reinterpret_cast<const float4*>(gain + d);
+            const float4 gb = *reinterpret_cast<const float4*>(gain + d + 64);
+            const float4 co = *reinterpret_cast<const float4*>(cs + d);
+            const float4 si = *reinterpret_cast<const float4*>(sn + d);
+            const float gav[4] = {ga.x, ga.y, ga.z, ga.w}, gbv[4] = {gb.x, gb.y, gb.z, gb.w};
+            const float cov[4] = {co.x, co.y, co.z, co.w}, siv[4] = {si.x, si.y, si.z, si.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float av = __uint_as_float(a16[i + e]) * rs * gav[e];
+              const float bv = __uint_as_float(b16[i + e]) * rs * gbv[e];
+              a16[i + e] = __float_as_uint(av * cov[e] - bv * siv[e]);  // low half of the pair
+              b16[i + e] = __float_as_uint(bv * cov[e] + av * siv[e]);  // high half
+            }
           }
-          store_row32_f16(orow + 32 * c, lo);
-          store_row32_f16(orow + 64 + 32 * c, hi);
+          uint4* lo4 = reinterpret_cast<uint4*>(orow + 16 * c);
+          uint4* hi4 = reinterpret_cast<uint4*>(orow + 64 + 16 * c);
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const float* fa = reinterpret_cast<const float*>(a16) + 8 * q;
+            const float* fb = reinterpret_cast<const float*>(b16) + 8 * q;
+            lo4[q] = make_uint4(pack_half2(fa[0], fa[1]), pack_half2(fa[2], fa[3]), pack_half2(fa[4], fa[5]),
+                                pack_half2(fa[6], fa[7]));
+            hi4[q] = make_uint4(pack_half2(fb[0], fb[1]), pack_half2(fb[2], fb[3]), pack_half2(fb[4], fb[5]),
+                                pack_half2(fb[6], fb[7]));
+          }
         }
       } else {
 #pragma unroll 1
@@ -260,7 +288,13 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
           tmem_ld_wait();
           if (!row_ok) continue;
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * rs * gain[32 * c + i];
+          for (int i = 0; i < 32; i += 4) {
+            const float4 gq = *reinterpret_cast<const float4*>(gain + 32 * c + i);
+            v[i] = __uint_as_float(r[i]) * rs * gq.x;
+            v[i + 1] = __uint_as_float(r[i + 1]) * rs * gq.y;
+            v[i + 2] = __uint_as_float(r[i + 2]) * rs * gq.z;
+            v[i + 3] = __uint_as_float(r[i + 3]) * rs * gq.w;
+          }
           store_row32_f16(orow + 32 * c, v);
         }
       }
@@ -287,12 +321,13 @@ template <int FMT, int EPI>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                 const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
-                const __grid_constant__ CUtensorMap tmMin, const KParams p) {
+                const __grid_constant__ CUtensorMap tmMin, const __grid_constant__ CUtensorMap tmX, const KParams p) {
   using C = Cfg<FMT>;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::STAGE_BYTES);
+  uint8_t* out_stage = smem + S * C::STAGE_BYTES;  // 1024-aligned
+  uint64_t* bars = reinterpret_cast<uint64_t*>(out_stage + C::OUT_STAGE);
   uint64_t* full = bars;            // TMA data landed        (count 1 + tx)
   uint64_t* dqfull = bars + S;      // dequantised tile ready (count DQ_WARPS)
   uint64_t* empty = bars + 2 * S;   // MMAs done with stage   (count 1, tcgen05.commit)
@@ -329,6 +364,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     prefetch_tmap(&tmW);
     if (p.nkb1 < p.nkb) prefetch_tmap(&tmA2);
     if (FMT != WF_F16) prefetch_tmap(&tmS);
+    if (EPI == EPI_RESID) prefetch_tmap(&tmX);
   }
   tc_fence_before();
   __syncthreads();
@@ -432,10 +468,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int acc = ti & 1;
       if (!mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 106)) { ok = false; break; }
       tc_fence_after();
-      epilogue_tile<EPI>(p, tmem + acc * BN, m0, n0, warp, lane);
+      epilogue_tile<EPI>(p, tmem + acc * BN, m0, n0, warp, lane, &tmX, out_stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+    if constexpr (EPI == EPI_RESID) {
+      if (threadIdx.x == 0) bulk_wait<0>();  // reductions complete before the CTA's shared memory goes away
     }
   }
 
@@ -503,7 +542,7 @@ int sm_count() {
 template <int FMT, int EPI>
 static cudaError_t launch_t(const GemmArgs& a, const KParams& p, const CUtensorMap& tA, const CUtensorMap& tA2,
                             const CUtensorMap& tW, const CUtensorMap& tS, const CUtensorMap& tMin,
-                            cudaStream_t s) {
+                            const CUtensorMap& tX, cudaStream_t s) {
   using C = Cfg<FMT>;
   static uint64_t attr_set = 0;  // one bit per device
   int dev = 0;
@@ -516,20 +555,20 @@ static cudaError_t launch_t(const GemmArgs& a, const KParams& p, const CUtensorM
   int grid = sm_count();
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
   if (p.num_tiles < grid) grid = p.num_tiles;
-  gemm_kernel<FMT, EPI><<<grid, GEMM_THREADS, C::SMEM, s>>>(tA, tA2, tW, tS, tMin, p);
+  gemm_kernel<FMT, EPI><<<grid, GEMM_THREADS, C::SMEM, s>>>(tA, tA2, tW, tS, tMin, tX, p);
   return cudaGetLastError();
 }
 
 template <int FMT>
 static cudaError_t launch_fmt(const GemmArgs& a, const KParams& p, const CUtensorMap& tA, const CUtensorMap& tA2,
                               const CUtensorMap& tW, const CUtensorMap& tS, const CUtensorMap& tMin,
-                              cudaStream_t s) {
+                              const CUtensorMap& tX, cudaStream_t s) {
   switch (a.epi) {
-    case EPI_STORE: return launch_t<FMT, EPI_STORE>(a, p, tA, tA2, tW, tS, tMin, s);
-    case EPI_RESID: return launch_t<FMT, EPI_RESID>(a, p, tA, tA2, tW, tS, tMin, s);
-    case EPI_GELU: return launch_t<FMT, EPI_GELU>(a, p, tA, tA2, tW, tS, tMin, s);
-    case EPI_RMS: return launch_t<FMT, EPI_RMS>(a, p, tA, tA2, tW, tS, tMin, s);
-    case EPI_SITU: return launch_t<FMT, EPI_SITU>(a, p, tA, tA2, tW, tS, tMin, s);
+    case EPI_STORE: return launch_t<FMT, EPI_STORE>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+    case EPI_RESID: return launch_t<FMT, EPI_RESID>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+    case EPI_GELU: return launch_t<FMT, EPI_GELU>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+    case EPI_RMS: return launch_t<FMT, EPI_RMS>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+    case EPI_SITU: return launch_t<FMT, EPI_SITU>(a, p, tA, tA2, tW, tS, tMin, tX, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -540,16 +579,21 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   const int N = W->N, K = W->K;
   if (K % BK || a.K1 % BK || a.K1 <= 0 || a.K1 > K || N % 32) return cudaErrorInvalidValue;
   if (a.K1 < K && (!a.A2 || a.lda2 < K - a.K1)) return cudaErrorInvalidValue;
-  if ((a.epi == EPI_RMS || a.epi == EPI_SITU) && N % BN) return cudaErrorInvalidValue;
+  if ((a.epi == EPI_RMS && N % 128) || (a.epi == EPI_SITU && N % BN)) return cudaErrorInvalidValue;
   if (a.epi == EPI_RESID && (!a.x || !a.gate)) return cudaErrorInvalidValue;
   if (a.epi != EPI_RESID && !a.out) return cudaErrorInvalidValue;
   if (W->fmt == WF_Q8 && W->group != 32 && W->group != 64) return cudaErrorInvalidValue;
   if ((W->fmt == WF_Q4 || W->fmt == WF_Q4A) && W->group != 32) return cudaErrorInvalidValue;
 
-  CUtensorMap tA, tA2, tW, tS, tMin;
+  CUtensorMap tA, tA2, tW, tS, tMin, tX;
   memset(&tA2, 0, sizeof tA2);
   memset(&tS, 0, sizeof tS);
   memset(&tMin, 0, sizeof tMin);
+  memset(&tX, 0, sizeof tX);
+  if (a.epi == EPI_RESID &&
+      !make_tmap_2d(&tX, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.x, N, a.M, static_cast<uint64_t>(a.ldx) * 4, 32, BM,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
   if (!make_tmap_2d(&tA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.A, a.K1, a.M, static_cast<uint64_t>(a.lda) * 2, BK,
                     BM, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
@@ -605,10 +649,10 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   if ((p.rope0 || p.rope1) && (!p.cosT || !p.sinT)) return cudaErrorInvalidValue;
 
   switch (W->fmt) {
-    case WF_F16: return launch_fmt<WF_F16>(a, p, tA, tA2, tW, tS, tMin, s);
-    case WF_Q8: return launch_fmt<WF_Q8>(a, p, tA, tA2, tW, tS, tMin, s);
-    case WF_Q4: return launch_fmt<WF_Q4>(a, p, tA, tA2, tW, tS, tMin, s);
-    case WF_Q4A: return launch_fmt<WF_Q4A>(a, p, tA, tA2, tW, tS, tMin, s);
+    case WF_F16: return launch_fmt<WF_F16>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+    case WF_Q8: return launch_fmt<WF_Q8>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+    case WF_Q4: return launch_fmt<WF_Q4>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+    case WF_Q4A: return launch_fmt<WF_Q4A>(a, p, tA, tA2, tW, tS, tMin, tX, s);
   }
   return cudaErrorInvalidValue;
 }
