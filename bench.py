@@ -5,16 +5,16 @@ python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--b
 Workload (configs[2] of BASELINE.json): 36 blocks (hidden 2048, 16 heads x 128, 1536 image tokens =
 32x48 patches, cross-attention to 256 text tokens of width 1024, GELU MLP 8192), int8 weights in
 groups of 64 along K with fp16 scales, 4 denoising steps, batch 8 images split over the N ranks
-(strong scaling, no collective on the data path). One bench step = the full 4-step denoise of the
-rank's images: per denoising step the AdaLN modulation of all 36 blocks from that step's timestep
-embedding, then the 36-block chain (one CUDA graph) — the per-block hot path end to end.
-The prelude/final-layer glue (x_embedder, final layer, Euler update) is not in the step.
+(strong scaling, no collective on the data path). One bench step = one full 4-step sample of the
+rank's images through hx_anima_sample (one CUDA graph): timestep embeddings, then per denoising step
+patchify + x_embedder, the AdaLN modulation and forward of all 36 blocks, final layer, unpatchify
+and the Euler update of the 16-channel 64x96 latent (animad.cpp:423-492 on the GPU).
 
 Timing: CUDA events on the runtime's stream, barrier + synchronize around the K timed steps, max
 over ranks. The weights (2.8 GB) are far larger than L2 (126 MB), so every step streams them from
-HBM ("inputs larger than L2"). e2e: the same steps through the C ABI with host buffers — pinned
-host -> device copy of the token state and text context, 4 chained denoise steps, device -> host
-read of the result, wall clock.
+HBM ("inputs larger than L2"). e2e: the same sample through the C ABI with host buffers — pinned
+host -> device copy of the initial latents and text contexts, the 4-step sample, device -> host read
+of the final latents, wall clock.
 """
 import argparse
 import json
@@ -179,6 +179,14 @@ def synth_weights(h, rt, torch, dev, seed):
     return wfds, keep
 
 
+def synth_glue(torch, dev, seed):
+    """Glue weights of the sampler (t_embedder, x_embedder, final layer), fp16 ~N(0, 0.02)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    n = lambda *s: (0.02 * torch.randn(*s, device=dev, generator=g)).half()
+    return {"t_norm": (1 + 0.02 * torch.randn(D, device=dev, generator=g)).half(), "t_lin1": n(D, D),
+            "t_lin2": n(3 * D, D), "x_emb": n(D, 68), "f_modA": n(256, D), "f_modB": n(2 * D, 256), "f_lin": n(64, D)}
+
+
 def time_q8_gemm(h, rt, torch, dev, M, iters=20):
     """Live roofline leg: the dominant kernel (mlp.layer1 q8 GEMM, M x 8192 x 2048, GELU epilogue)
     timed alone with CUDA events on the runtime's stream."""
@@ -223,27 +231,28 @@ def run_ours(args, rank, world, local_rank):
     bfd = h.buf_alloc(total)
     A = rt.A
     rng = np.random.default_rng(4321 + rank)
-    x0 = rng.standard_normal((B, T, D), dtype=np.float32)
+    LH, LW = 64, 96  # 512x768 image -> 64x96 latent -> 32x48 patches
+    lat0 = rng.standard_normal((B, 16, LH, LW), dtype=np.float32)
     ctx0 = rng.standard_normal((B, C, CD), dtype=np.float32).astype(np.float16)
-    cos, sin = rt.rope_anima(32, 48, 10000.0, T)
+    cos, sin = rt.rope_anima(LH // 2, LW // 2, 10000.0, T)
     h.buf_write(bfd, meta[A["COS"]], cos)
     h.buf_write(bfd, meta[A["SIN"]], sin)
-    # per-denoise-step timestep embeddings (synthetic inputs of the modulation mat-vecs)
-    gen = torch.Generator(device=dev).manual_seed(4321 + rank)
-    emb = torch.randn(NSTEP, D, device=dev, generator=gen)
-    lora = 0.1 * torch.randn(NSTEP, 3 * D, device=dev, generator=gen)
-    xnbytes = B * T * D * 4
+    glue = synth_glue(torch, dev, 777)
+    gfd = h.glue_load(D, glue["t_norm"], glue["t_lin1"], glue["t_lin2"], glue["x_emb"], glue["f_modA"],
+                      glue["f_modB"], glue["f_lin"])
+    lat_fd = h.buf_alloc(lat0.nbytes)
+    lat_ptr = h.buf_ptr(lat_fd)
+    latnbytes = lat0.nbytes
     cnbytes = B * C * CD * 2
 
     def one_step():
-        for i in range(NSTEP):
-            h.chain(meta, wfds, bfd, emb_dev=emb[i], lora_dev=lora[i], use_graph=True)
+        h.anima_sample(gfd, meta, wfds, bfd, lat_ptr, LH, LW, NSTEP, use_graph=True)
 
     def reset_state():
-        h.buf_write(bfd, meta[A["X"]], x0)
+        h.buf_write(lat_fd, 0, lat0)
         h.buf_write(bfd, meta[A["CTX"]], ctx0)
 
-    # warm-up (captures the four chain graphs)
+    # warm-up (captures the sample graph)
     reset_state()
     for _ in range(max(args.warmup, 3)):
         one_step()
@@ -269,19 +278,19 @@ def run_ours(args, rank, world, local_rank):
     if h.status() != 0:
         raise RuntimeError("device wait timed out in the timed region")
 
-    # e2e through the C ABI with host buffers: pinned host -> blob, 4 steps, blob -> host
-    host_x = torch.empty(B * T * D, dtype=torch.float32).pin_memory()
-    host_x.copy_(torch.from_numpy(x0.reshape(-1)))
+    # e2e through the C ABI with host buffers: pinned host -> device latents and contexts, sample, read back
+    host_lat = torch.empty(lat0.size, dtype=torch.float32).pin_memory()
+    host_lat.copy_(torch.from_numpy(lat0.reshape(-1)))
     host_c = torch.empty(B * C * CD, dtype=torch.float16).pin_memory()
     host_c.copy_(torch.from_numpy(ctx0.reshape(-1)))
-    host_out = torch.empty(B * T * D, dtype=torch.float32).pin_memory()
+    host_out = torch.empty(lat0.size, dtype=torch.float32).pin_memory()
     lib = rt.lib()
 
     def e2e_step():
-        lib.hx_buf_write(h.h, bfd, meta[A["X"]], host_x.data_ptr(), xnbytes)
+        lib.hx_buf_write(h.h, lat_fd, 0, host_lat.data_ptr(), latnbytes)
         lib.hx_buf_write(h.h, bfd, meta[A["CTX"]], host_c.data_ptr(), cnbytes)
         one_step()
-        lib.hx_buf_read(h.h, bfd, meta[A["X"]], host_out.data_ptr(), xnbytes)
+        lib.hx_buf_read(h.h, lat_fd, 0, host_out.data_ptr(), latnbytes)
 
     e2e_step()
     if dist:
@@ -305,6 +314,7 @@ def run_ours(args, rank, world, local_rank):
     tf, gms = time_q8_gemm(h, rt, torch, dev, B * T)
     traffic = _profile_traffic()
     launches_per_block = 3 + 7 + 2 + 2  # LN x3, GEMM x7, attention x2, modulation mat-vecs x2
+    launches_per_sample = 5 + NSTEP * (5 + launches_per_block * NBLK)  # temb + 4 mat-vecs; per step glue + blocks
     line = None
     if rank == 0:
         cpu_s, cores = cpu_block_seconds(reps=1, threads=os.cpu_count())
@@ -318,16 +328,17 @@ def run_ours(args, rank, world, local_rank):
                        "global_batch": images, "per_rank_batch": B, "tokens": T, "ctx_tokens": C, "hidden": D,
                        "heads": HEADS, "ffn": F, "weights": "int8 g64 + fp16 scales", "blocks": NBLK, "steps": NSTEP,
                        "parallelism": f"dp{world} (image batch, no collective)",
-                       "l2": "weights 2.8 GB > L2: every step streams from HBM", "glue": "not included",
+                       "l2": "weights 2.8 GB > L2: every step streams from HBM",
+                       "glue": "on GPU: timestep embedding, x_embedder, final layer, Euler (animad.cpp:423-492)",
                        "seed": 1234},
             "effective_tflops": flop_step / (ms * 1e-3) / 1e12,
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peak_tf, "unit": "TFLOP/s", "frac": tf / peak_tf,
                          "traffic": traffic, "kernel": f"q8 GEMM {B * T}x{F}x{D} GELU epilogue",
                          "peak_kind": f"bf16 dense burst, {peak_kind}", "launch_ms": gms},
             "clocks": clk.summary(),
-            "e2e": {"value": images / e2e_s, "unit": "images/s", "h2d_bytes_per_step": (xnbytes + cnbytes) * world,
-                    "d2h_bytes_per_step": xnbytes * world},
-            "gpu_launches": launches_per_block * NBLK * NSTEP,
+            "e2e": {"value": images / e2e_s, "unit": "images/s", "h2d_bytes_per_step": (latnbytes + cnbytes) * world,
+                    "d2h_bytes_per_step": latnbytes * world},
+            "gpu_launches": launches_per_sample,
             "cpu_baseline": {"value": cpu_img_s, "unit": "images/s", "cores": cores, "kind": "port",
                              "sample": "oracle Anima block (torch fp32) at T=1536, 1 image, 1 block timed after 1 warm-up; images/s = 1/(t_block*36*4)"},
         }

@@ -49,6 +49,27 @@ struct Buf {
   size_t bytes = 0;
 };
 
+struct Glue {
+  int D = 0;
+  __half *t_norm = nullptr, *t_lin1 = nullptr, *t_lin2 = nullptr, *x_emb = nullptr /* [D][128], K padded */,
+         *f_modA = nullptr, *f_modB = nullptr, *f_lin = nullptr;
+  std::vector<void*> owned;
+};
+
+// Device scratch of the sampler, grown on demand (never inside a graph capture).
+struct SampleScratch {
+  int S = 0, D = 0;
+  size_t rows = 0;
+  float *tp = nullptr, *emb = nullptr, *tmp = nullptr, *lora = nullptr, *h256 = nullptr, *fmod = nullptr,
+        *y = nullptr;
+  __half* P = nullptr;
+  void release() {
+    for (void* p : {(void*)tp, (void*)emb, (void*)tmp, (void*)lora, (void*)h256, (void*)fmod, (void*)y, (void*)P})
+      cudaFree(p);
+    *this = SampleScratch();
+  }
+};
+
 struct ChainGraph {
   std::vector<int64_t> key;
   cudaGraphExec_t exec = nullptr;
@@ -71,6 +92,8 @@ struct hx_ctx {
   cudaEvent_t ev[34] = {};
   std::vector<ChainGraph> graphs;
   uint64_t graph_clock = 0;
+  std::map<int, std::unique_ptr<Glue>> glues;
+  SampleScratch ss;
   std::mutex mu;
   void drop_graphs() {
     for (auto& g : graphs)
@@ -576,6 +599,77 @@ int run_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, c
                                    : moss_block(h, W, meta, blob, mod_dev, st);
 }
 
+// per-block modulation vectors in h->modscratch (allocated by the caller before any capture)
+constexpr size_t kModStride(int D) { return 9ull * D + 3 * 256; }
+
+int chain_body(hx_ctx* h, const std::vector<const Weights*>& ws, const int32_t* m, uint8_t* blob, const float* mods_dev,
+               const float* emb_dev, const float* lora_dev, uint32_t skipmask) {
+  const int model = ws[0]->model, D = ws[0]->D;
+  const size_t per = model == HX_MODEL_ANIMA ? kModStride(D) : 6ull * D;
+  for (size_t k = 0; k < ws.size(); ++k) {
+    if ((skipmask >> k) & 1) continue;
+    const float* md;
+    if (mods_dev) {
+      md = mods_dev + k * (model == HX_MODEL_ANIMA ? 9ull * D : 6ull * D);
+    } else {
+      float* out = h->modscratch + per * k;
+      if (modulation_launch(ws[k]->modA, ws[k]->modB, emb_dev, lora_dev, out, 3, D, 256, 3 * D, h->stream) !=
+          cudaSuccess)
+        return HX_E_CUDA;
+      md = out;
+    }
+    Stage st{h, 0, 0, 0};
+    if (int r = run_block(h, *ws[k], m, blob, md, st)) return r;
+  }
+  return HX_OK;
+}
+
+int ensure_modscratch(hx_ctx* h, size_t floats) {
+  if (h->modscratch_floats >= floats) return HX_OK;
+  cudaStreamSynchronize(h->stream);
+  cudaFree(h->modscratch);
+  h->modscratch = nullptr;
+  h->modscratch_floats = 0;
+  if (cudaMalloc(&h->modscratch, floats * 4) != cudaSuccess) return HX_E_CUDA;
+  h->modscratch_floats = floats;
+  h->drop_graphs();
+  return HX_OK;
+}
+
+// run `body` directly, or captured once per key and replayed
+template <class F>
+int run_graphed(hx_ctx* h, std::vector<int64_t> key, F&& body, bool use_graph) {
+  if (!use_graph) return body();
+  key.push_back(reinterpret_cast<int64_t>(h->stream));
+  ChainGraph* hit = nullptr;
+  for (auto& g : h->graphs)
+    if (g.key == key) hit = &g;
+  if (!hit) {
+    cudaGraph_t graph = nullptr;
+    if (cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeRelaxed) != cudaSuccess) return HX_E_CUDA;
+    int r = body();
+    cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
+    if (r || ce != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      return r ? r : HX_E_CUDA;
+    }
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return HX_E_CUDA;
+    if (h->graphs.size() >= kMaxGraphs) {  // evict the least recently used
+      auto lru = std::min_element(h->graphs.begin(), h->graphs.end(),
+                                  [](const ChainGraph& a, const ChainGraph& b) { return a.last_use < b.last_use; });
+      cudaGraphExecDestroy(lru->exec);
+      h->graphs.erase(lru);
+    }
+    h->graphs.push_back(ChainGraph{key, exec, 0});
+    hit = &h->graphs.back();
+  }
+  hit->last_use = ++h->graph_clock;
+  return cudaGraphLaunch(hit->exec, h->stream) == cudaSuccess ? HX_OK : HX_E_CUDA;
+}
+
 std::vector<int32_t> full_meta(const int32_t* meta, int nmeta, int model) {
   const int n = model == HX_MODEL_ANIMA ? HX_A_NMETA_EXT : HX_S_NMETA_EXT;
   std::vector<int32_t> m(std::max(n, nmeta), 0);
@@ -621,6 +715,9 @@ int hx_close(hx_handle hh) {
     for (auto& kv : h->weights)
       for (void* p : kv.second->owned) cudaFree(p);
     cudaFree(h->modscratch);
+    for (auto& kv : h->glues)
+      for (void* p : kv.second->owned) cudaFree(p);
+    h->ss.release();
     cudaFree(h->status);
     for (auto& e : h->ev) cudaEventDestroy(e);
     if (h->own_stream) cudaStreamDestroy(h->stream);
@@ -953,81 +1050,172 @@ int hx_chain(hx_handle hh, const int32_t* meta, int nmeta, const int* wfds, int 
   std::vector<int32_t> m = full_meta(meta, nmeta, model);
   for (int k = 0; k < count; ++k)
     if (int r = check_meta(*ws[k], m.data(), static_cast<int>(m.size()), bi->second.bytes)) return (*rc = r);
-  const size_t per = model == HX_MODEL_ANIMA ? 9ull * D + 3 * 256 : 6ull * D;
   if (!mods_dev) {
     if (model != HX_MODEL_ANIMA || !emb_dev) return (*rc = HX_E_ARG);
     for (int k = 0; k < count; ++k)
       if (!ws[k]->modA || !ws[k]->modB) return (*rc = HX_E_ARG);
   }
   DevGuard g(h->device);
-  if (!mods_dev && h->modscratch_floats < per * count) {
-    cudaStreamSynchronize(h->stream);
-    cudaFree(h->modscratch);
-    h->modscratch = nullptr;
-    h->modscratch_floats = 0;
-    if (cudaMalloc(&h->modscratch, per * count * 4) != cudaSuccess) return (*rc = HX_E_CUDA);
-    h->modscratch_floats = per * count;
-    h->drop_graphs();
-  }
+  if (!mods_dev)
+    if (int r = ensure_modscratch(h, kModStride(D) * count)) return (*rc = r);
   uint8_t* blob = static_cast<uint8_t*>(bi->second.ptr);
+  std::vector<int64_t> key(m.begin(), m.end());
+  for (int k = 0; k < count; ++k) key.push_back(wfds[k]);
+  for (int64_t v : {int64_t(1), int64_t(bfd), reinterpret_cast<int64_t>(mods_dev), reinterpret_cast<int64_t>(emb_dev),
+                    reinterpret_cast<int64_t>(lora_dev), int64_t(skipmask)})
+    key.push_back(v);
+  const int r = run_graphed(
+      h, key, [&] { return chain_body(h, ws, m.data(), blob, mods_dev, emb_dev, lora_dev, skipmask); },
+      use_graph != 0);
+  return (*rc = r);
+}
+
+// ---------------------------------------------------------------- glue + sampler
+int hx_glue_load(hx_handle hh, const hx_anima_glue_desc* d, int* gfd) {
+  hx_ctx* h = H(hh);
+  if (!h || !d || !gfd || d->D <= 0 || d->D % 256) return HX_E_ARG;
+  if (!d->t_norm || !d->t_lin1 || !d->t_lin2 || !d->x_emb || !d->f_modA || !d->f_modB || !d->f_lin) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  DevGuard g(h->device);
+  auto G = std::make_unique<Glue>();
+  const size_t D = d->D;
+  auto copy = [&](const void* src, size_t elems, __half** dst) -> int {
+    void* p = nullptr;
+    CK(cudaMalloc(&p, elems * 2));
+    G->owned.push_back(p);
+    CK(cudaMemcpyAsync(p, src, elems * 2, cudaMemcpyDeviceToDevice, h->stream));
+    *dst = static_cast<__half*>(p);
+    return HX_OK;
+  };
+  int r;
+  if ((r = copy(d->t_norm, D, &G->t_norm)) || (r = copy(d->t_lin1, D * D, &G->t_lin1)) ||
+      (r = copy(d->t_lin2, 3 * D * D, &G->t_lin2)) || (r = copy(d->f_modA, 256 * D, &G->f_modA)) ||
+      (r = copy(d->f_modB, 2 * D * 256, &G->f_modB)) || (r = copy(d->f_lin, 64 * D, &G->f_lin))) {
+    for (void* p : G->owned) cudaFree(p);
+    return r;
+  }
+  void* xe = nullptr;
+  if (cudaMalloc(&xe, D * 128 * 2) != cudaSuccess) {
+    for (void* p : G->owned) cudaFree(p);
+    return HX_E_CUDA;
+  }
+  G->owned.push_back(xe);
+  G->x_emb = static_cast<__half*>(xe);
+  if (pad_cols_launch(static_cast<const __half*>(d->x_emb), G->x_emb, static_cast<int>(D), 68, 128, h->stream) !=
+          cudaSuccess ||
+      cudaStreamSynchronize(h->stream) != cudaSuccess) {
+    for (void* p : G->owned) cudaFree(p);
+    return HX_E_CUDA;
+  }
+  G->D = d->D;
+  *gfd = h->next_fd++;
+  h->glues[*gfd] = std::move(G);
+  return HX_OK;
+}
+
+int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const int* wfds, int nblk, int bfd,
+                    float* latent, int lat_h, int lat_w, int nsteps, const float* sigmas, int use_graph,
+                    int32_t* rc) {
+  hx_ctx* h = H(hh);
+  if (!h || !rc || !meta || !wfds || nblk <= 0 || !latent) return HX_E_ARG;
+  *rc = HX_OK;
+  if (nsteps <= 0 || nsteps > 8 || lat_h % 2 || lat_w % 2) return (*rc = HX_E_ARG);
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto gi = h->glues.find(gfd);
+  if (gi == h->glues.end()) return (*rc = HX_E_ARG);
+  const Glue& G = *gi->second;
+  auto bi = h->bufs.find(bfd);
+  if (bi == h->bufs.end()) return (*rc = HX_E_NOBLOB);
+  std::vector<const Weights*> ws(nblk);
+  for (int k = 0; k < nblk; ++k) {
+    auto wi = h->weights.find(wfds[k]);
+    if (wi == h->weights.end()) return (*rc = HX_E_NOWEIGHTS);
+    ws[k] = wi->second.get();
+    if (ws[k]->model != HX_MODEL_ANIMA || ws[k]->D != G.D || !ws[k]->modA || !ws[k]->modB) return (*rc = HX_E_ARG);
+  }
+  std::vector<int32_t> m = full_meta(meta, nmeta, HX_MODEL_ANIMA);
+  for (int k = 0; k < nblk; ++k)
+    if (int r = check_meta(*ws[k], m.data(), static_cast<int>(m.size()), bi->second.bytes)) return (*rc = r);
+  const int D = G.D, T = m[HX_A_NTOK], B = m[HX_A_BATCH] > 0 ? m[HX_A_BATCH] : 1;
+  if ((lat_h / 2) * (lat_w / 2) != T) return (*rc = HX_E_ARG);
+  Sigmas sg{};
+  float sig[9];
+  for (int i = 0; i <= nsteps; ++i) {
+    if (sigmas) {
+      sig[i] = sigmas[i];
+    } else if (i == nsteps) {
+      sig[i] = 0.f;
+    } else {  // animad.cpp:397-399
+      const double sv = nsteps > 1 ? 1.0 - (1.0 - 0.001) * i / (nsteps - 1) : 1.0;
+      sig[i] = static_cast<float>(3 * sv / (1 + 2 * sv));
+    }
+  }
+  for (int i = 0; i < nsteps; ++i) sg.s[i] = sig[i];
+  DevGuard g(h->device);
+  const size_t rows = static_cast<size_t>(B) * T;
+  SampleScratch& sc = h->ss;
+  if (sc.S < nsteps || sc.D != D || sc.rows < rows) {
+    cudaStreamSynchronize(h->stream);
+    h->drop_graphs();
+    sc.release();
+    const size_t S = 8;
+    bool ok = cudaMalloc(&sc.tp, S * D * 4) == cudaSuccess && cudaMalloc(&sc.emb, S * D * 4) == cudaSuccess &&
+              cudaMalloc(&sc.tmp, S * D * 4) == cudaSuccess && cudaMalloc(&sc.lora, S * 3 * D * 4) == cudaSuccess &&
+              cudaMalloc(&sc.h256, S * 256 * 4) == cudaSuccess && cudaMalloc(&sc.fmod, S * 2 * D * 4) == cudaSuccess &&
+              cudaMalloc(&sc.y, rows * 64 * 4) == cudaSuccess && cudaMalloc(&sc.P, rows * 128 * 2) == cudaSuccess;
+    if (!ok) {
+      sc.release();
+      return (*rc = HX_E_CUDA);
+    }
+    sc.S = static_cast<int>(S);
+    sc.D = D;
+    sc.rows = rows;
+  }
+  if (int r = ensure_modscratch(h, kModStride(D) * nblk)) return (*rc = r);
+  uint8_t* blob = static_cast<uint8_t*>(bi->second.ptr);
+  float* x = reinterpret_cast<float*>(blob + m[HX_A_X]);
+  __half* hbuf = hptr(blob, m[HX_A_H]);
+  cudaStream_t s = h->stream;
   auto body = [&]() -> int {
-    for (int k = 0; k < count; ++k) {
-      if ((skipmask >> k) & 1) continue;
-      const float* md;
-      if (mods_dev) {
-        md = mods_dev + static_cast<size_t>(k) * (model == HX_MODEL_ANIMA ? 9 * D : 6 * D);
-      } else {
-        float* out = h->modscratch + per * k;
-        if (modulation_launch(ws[k]->modA, ws[k]->modB, emb_dev, lora_dev, out, 3, D, 256, 3 * D, h->stream) !=
-            cudaSuccess)
-          return HX_E_CUDA;
-        md = out;
-      }
-      Stage st{h, 0, 0, 0};
-      if (int r = run_block(h, *ws[k], m.data(), blob, md, st)) return r;
+    const int S = nsteps;
+    CKL(temb_launch(sg, S, D, G.t_norm, sc.tp, sc.emb, s));
+    CKL(gemv_rows_launch(G.t_lin1, sc.tp, sc.tmp, S, D, D, 0, nullptr, 0, D, s));
+    CKL(gemv_rows_launch(G.t_lin2, sc.tmp, sc.lora, S, D, 3 * D, 1, nullptr, 0, 3 * D, s));
+    CKL(gemv_rows_launch(G.f_modA, sc.emb, sc.h256, S, D, 256, 1, nullptr, 0, 256, s));
+    CKL(gemv_rows_launch(G.f_modB, sc.h256, sc.fmod, S, 256, 2 * D, 0, sc.lora, 3 * D, 2 * D, s));
+    DevMat xe, fl;
+    xe.fmt = WF_F16; xe.N = D; xe.K = 128; xe.w = G.x_emb;
+    fl.fmt = WF_F16; fl.N = 64; fl.K = D; fl.w = G.f_lin;
+    for (int i = 0; i < S; ++i) {
+      CKL(patchify_launch(latent, sc.P, B, 16, lat_h, lat_w, 128, s));
+      GemmArgs ge = gargs(h, sc.P, 128, static_cast<int>(rows), &xe, EPI_STORE32);
+      ge.x = x;
+      ge.ldx = D;
+      CKL(gemm_launch(ge, s));
+      if (int r = chain_body(h, ws, m.data(), blob, nullptr, sc.emb + static_cast<size_t>(i) * D,
+                             sc.lora + static_cast<size_t>(i) * 3 * D, 0))
+        return r;
+      const float* fm = sc.fmod + static_cast<size_t>(i) * 2 * D;
+      CKL(lnmod_launch(x, hbuf, static_cast<int>(rows), D, fm, fm + D, 0, T, 1e-6f, s));
+      GemmArgs gf = gargs(h, hbuf, D, static_cast<int>(rows), &fl, EPI_STORE32);
+      gf.x = sc.y;
+      gf.ldx = 64;
+      CKL(gemm_launch(gf, s));
+      CKL(unpatch_euler_launch(sc.y, latent, B, 16, lat_h, lat_w, 64, sig[i + 1] - sig[i], s));
     }
     return HX_OK;
   };
-  if (!use_graph) {
-    int r = body();
-    return (*rc = r);
-  }
   std::vector<int64_t> key(m.begin(), m.end());
-  for (int k = 0; k < count; ++k) key.push_back(wfds[k]);
-  key.push_back(bfd);
-  key.push_back(reinterpret_cast<int64_t>(mods_dev));
-  key.push_back(reinterpret_cast<int64_t>(emb_dev));
-  key.push_back(reinterpret_cast<int64_t>(lora_dev));
-  key.push_back(skipmask);
-  key.push_back(reinterpret_cast<int64_t>(h->stream));
-  ChainGraph* hit = nullptr;
-  for (auto& g : h->graphs)
-    if (g.key == key) hit = &g;
-  if (!hit) {
-    cudaGraph_t graph = nullptr;
-    if (cudaStreamBeginCapture(h->stream, cudaStreamCaptureModeRelaxed) != cudaSuccess) return (*rc = HX_E_CUDA);
-    int r = body();
-    cudaError_t ce = cudaStreamEndCapture(h->stream, &graph);
-    if (r || ce != cudaSuccess) {
-      if (graph) cudaGraphDestroy(graph);
-      return (*rc = r ? r : HX_E_CUDA);
-    }
-    cudaGraphExec_t exec = nullptr;
-    cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
-    cudaGraphDestroy(graph);
-    if (ie != cudaSuccess) return (*rc = HX_E_CUDA);
-    if (h->graphs.size() >= kMaxGraphs) {  // evict the least recently used
-      auto lru = std::min_element(h->graphs.begin(), h->graphs.end(),
-                                  [](const ChainGraph& a, const ChainGraph& b) { return a.last_use < b.last_use; });
-      cudaGraphExecDestroy(lru->exec);
-      h->graphs.erase(lru);
-    }
-    h->graphs.push_back(ChainGraph{key, exec, 0});
-    hit = &h->graphs.back();
+  for (int k = 0; k < nblk; ++k) key.push_back(wfds[k]);
+  for (int64_t v : {int64_t(2), int64_t(gfd), int64_t(bfd), reinterpret_cast<int64_t>(latent), int64_t(lat_h),
+                    int64_t(lat_w), int64_t(nsteps)})
+    key.push_back(v);
+  for (int i = 0; i <= nsteps; ++i) {
+    int32_t bits;
+    std::memcpy(&bits, &sig[i], 4);
+    key.push_back(bits);
   }
-  hit->last_use = ++h->graph_clock;
-  if (cudaGraphLaunch(hit->exec, h->stream) != cudaSuccess) return (*rc = HX_E_CUDA);
-  return HX_OK;
+  return (*rc = run_graphed(h, key, body, use_graph != 0));
 }
 
 // ---------------------------------------------------------------- operator level

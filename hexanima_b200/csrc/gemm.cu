@@ -164,7 +164,21 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
   (void)tmX;
   uint32_t r[32];
   float v[32];
-  if constexpr (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_RESID) {
+  if constexpr (EPI == EPI_STORE32) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      const int n = n0 + 32 * c;
+      if (n >= p.N) break;
+      tmem_ld32(tl + 32 * c, r);
+      tmem_ld_wait();
+      if (!row_ok) continue;
+      float4* xr = reinterpret_cast<float4*>(p.x + static_cast<size_t>(m) * p.ldx + n);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        xr[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                            __uint_as_float(r[4 * q + 3]));
+    }
+  } else if constexpr (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_RESID) {
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       const int n = n0 + 32 * c;
@@ -569,6 +583,7 @@ static cudaError_t launch_fmt(const GemmArgs& a, const KParams& p, const CUtenso
     case EPI_GELU: return launch_t<FMT, EPI_GELU>(a, p, tA, tA2, tW, tS, tMin, tX, s);
     case EPI_RMS: return launch_t<FMT, EPI_RMS>(a, p, tA, tA2, tW, tS, tMin, tX, s);
     case EPI_SITU: return launch_t<FMT, EPI_SITU>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+    case EPI_STORE32: return launch_t<FMT, EPI_STORE32>(a, p, tA, tA2, tW, tS, tMin, tX, s);
   }
   return cudaErrorInvalidValue;
 }
@@ -581,7 +596,8 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   if (a.K1 < K && (!a.A2 || a.lda2 < K - a.K1)) return cudaErrorInvalidValue;
   if ((a.epi == EPI_RMS && N % 128) || (a.epi == EPI_SITU && N % BN)) return cudaErrorInvalidValue;
   if (a.epi == EPI_RESID && (!a.x || !a.gate)) return cudaErrorInvalidValue;
-  if (a.epi != EPI_RESID && !a.out) return cudaErrorInvalidValue;
+  if (a.epi == EPI_STORE32 && (!a.x || a.ldx % 4)) return cudaErrorInvalidValue;
+  if (a.epi != EPI_RESID && a.epi != EPI_STORE32 && !a.out) return cudaErrorInvalidValue;
   if (W->fmt == WF_Q8 && W->group != 32 && W->group != 64) return cudaErrorInvalidValue;
   if ((W->fmt == WF_Q4 || W->fmt == WF_Q4A) && W->group != 32) return cudaErrorInvalidValue;
 

@@ -18,6 +18,7 @@ enum Epi : int {
   EPI_GELU = 2,   // out16 = gelu_erf(acc)                      (mode 2)
   EPI_RMS = 3,    // per 128-col head: rms * gain (+ rope)      (mode 3)
   EPI_SITU = 5,   // tile cols [0,128) up, [128,256) gate -> 128 outputs   (mode 5)
+  EPI_STORE32 = 6,  // x32 = acc (fp32 output in the x / ldx fields; glue GEMMs)
 };
 
 // A weight matrix W[N][K] in device memory, in one of the WFmt layouts.
@@ -86,6 +87,18 @@ cudaError_t rmsmod_launch(const float* x, __half* h, int rows, int D, const floa
 cudaError_t modulation_launch(const __half* Aw, const __half* Bw, const float* emb, const float* lora, float* out,
                               int nsite, int D, int R, int O, cudaStream_t s);
 cudaError_t f32_to_f16_launch(const float* src, __half* dst, size_t n, cudaStream_t s);
+
+// per-step glue (glue.cu)
+struct Sigmas {
+  float s[8];
+};
+cudaError_t temb_launch(Sigmas sig, int S, int D, const __half* w_norm, float* tp, float* emb, cudaStream_t s);
+cudaError_t gemv_rows_launch(const __half* W, const float* X, float* Y, int S, int K, int O, int silu_in,
+                             const float* add, int add_ld, int y_ld, cudaStream_t s);
+cudaError_t patchify_launch(const float* lat, __half* P, int B, int C, int H, int W, int kpad, cudaStream_t s);
+cudaError_t unpatch_euler_launch(const float* y, float* lat, int B, int C, int H, int W, int ldy, float dt,
+                                 cudaStream_t s);
+cudaError_t pad_cols_launch(const __half* src, __half* dst, int rows, int cols, int ld_dst, cudaStream_t s);
 
 // weight repacking from the reference pack records (repack.cu)
 cudaError_t repack_tiles_launch(const uint8_t* rec, int nb, int kb, bool q8, void* dst, __half* scale, int row0,

@@ -24,7 +24,7 @@ ERRORS = {-1: "HX_E_ARG", -2: "HX_E_CUDA", -5: "HX_E_NOWEIGHTS", -6: "HX_E_NOBLO
 
 MODEL_ANIMA, MODEL_MOSS = 1, 2
 FMT_F16, FMT_Q8, FMT_Q4A, FMT_Q4 = 0, 1, 2, 3
-EPI_STORE, EPI_RESID, EPI_GELU, EPI_RMS, EPI_SITU = 0, 1, 2, 3, 5
+EPI_STORE, EPI_RESID, EPI_GELU, EPI_RMS, EPI_SITU, EPI_STORE32 = 0, 1, 2, 3, 5, 6
 (W_QKV, W_O, W_CQ, W_CKV, W_CO, W_M1, W_M2, W_Q, W_K, W_V, W_AQKV, W_AO, W_AUG, W_ADN) = range(14)
 NMATS = 14
 
@@ -70,6 +70,12 @@ class hx_weight_desc(ctypes.Structure):
                 ("modA", ctypes.c_void_p), ("modB", ctypes.c_void_p)]
 
 
+class hx_anima_glue_desc(ctypes.Structure):
+    _fields_ = [("D", ctypes.c_int), ("t_norm", ctypes.c_void_p), ("t_lin1", ctypes.c_void_p),
+                ("t_lin2", ctypes.c_void_p), ("x_emb", ctypes.c_void_p), ("f_modA", ctypes.c_void_p),
+                ("f_modB", ctypes.c_void_p), ("f_lin", ctypes.c_void_p)]
+
+
 class hx_gemm_desc(ctypes.Structure):
     _fields_ = [("a", ctypes.c_void_p), ("lda", ctypes.c_int), ("a2", ctypes.c_void_p), ("lda2", ctypes.c_int),
                 ("m", ctypes.c_int), ("k1", ctypes.c_int), ("w", hx_mat), ("epi", ctypes.c_int),
@@ -111,6 +117,8 @@ _SIGS = {
     "hx_mega_block": [_vp, _ip, _i, _i, _i, _vp, _i, _ip, _i, _ip],
     "hx_modulation": [_vp, _i, _vp, _vp, _vp],
     "hx_chain": [_vp, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _vp, _vp, ctypes.c_uint32, _i, _ip],
+    "hx_glue_load": [_vp, ctypes.POINTER(hx_anima_glue_desc), ctypes.POINTER(_i)],
+    "hx_anima_sample": [_vp, _i, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _i, _i, _i, _vp, _i, _ip],
     "hx_gemm": [_vp, ctypes.POINTER(hx_gemm_desc)],
     "hx_attention": [_vp, ctypes.POINTER(hx_attn_desc)],
     "hx_lnmod": [_vp, _vp, _vp, _i, _i, _vp, _vp, _l, _i, _f],
@@ -284,6 +292,27 @@ class Handle:
                            skipmask, 1 if use_graph else 0, ctypes.byref(rc))
         _check(r, "hx_chain")
         _check(rc.value, "hx_chain rc")
+
+    # -------------------------------------------------------------- glue + sampler
+    def glue_load(self, D, t_norm, t_lin1, t_lin2, x_emb, f_modA, f_modB, f_lin):
+        d = hx_anima_glue_desc(D, _ptr(t_norm), _ptr(t_lin1), _ptr(t_lin2), _ptr(x_emb), _ptr(f_modA), _ptr(f_modB),
+                               _ptr(f_lin))
+        g = ctypes.c_int()
+        _check(lib().hx_glue_load(self.h, ctypes.byref(d), ctypes.byref(g)), "hx_glue_load")
+        return g.value
+
+    def anima_sample(self, gfd, meta, wfds, bfd, latent_dev, lat_h, lat_w, nsteps=4, sigmas=None, use_graph=True):
+        m = (ctypes.c_int32 * len(meta))(*meta)
+        w = (ctypes.c_int * len(wfds))(*wfds)
+        rc = ctypes.c_int32()
+        sg = None
+        if sigmas is not None:
+            sarr = np.ascontiguousarray(sigmas, np.float32)
+            sg = sarr.ctypes.data
+        r = lib().hx_anima_sample(self.h, gfd, m, len(meta), w, len(wfds), bfd, _ptr(latent_dev), lat_h, lat_w, nsteps,
+                                  sg, 1 if use_graph else 0, ctypes.byref(rc))
+        _check(r, "hx_anima_sample")
+        _check(rc.value, "hx_anima_sample rc")
 
     # -------------------------------------------------------------- operators
     def gemm(self, a, m, mat, epi=EPI_STORE, lda=None, k1=0, a2=None, lda2=0, out=None, ldo=0, x=None, ldx=0,

@@ -184,6 +184,33 @@ HX_API int hx_chain(hx_handle h, const int32_t* meta, int nmeta, const int* wfds
              const float* mods_dev, const float* emb_dev, const float* lora_dev, uint32_t skipmask, int use_graph,
              int32_t* rc);
 
+/* ------------------------------------------------------------------ per-step glue and the sampler
+ * Anima step glue of phone/animad.cpp:423-492, on the GPU: timestep embedding (σ used directly as t,
+ * [cos | sin] with frequencies 10000^(-i/(D/2)), RMSNorm * t_embedding_norm), t_embedder
+ * lora = linear_2(silu(linear_1(tp))), patchify (16 latent channels + a zero 17th, feature c*4+a*2+b),
+ * x_embedder 68 -> D, the block chain, final layer (LayerNorm * (1 + scale) + shift with
+ * [shift | scale] = B_f (A_f silu(emb)) + lora[0:2D], linear D -> 64), unpatchify, Euler update. */
+typedef struct {
+  int D;                /* hidden size (2048) */
+  const void* t_norm;   /* fp16 [D]       t_embedding_norm.weight */
+  const void* t_lin1;   /* fp16 [D][D]    t_embedder.1.linear_1.weight */
+  const void* t_lin2;   /* fp16 [3D][D]   t_embedder.1.linear_2.weight */
+  const void* x_emb;    /* fp16 [D][68]   x_embedder.proj.1.weight */
+  const void* f_modA;   /* fp16 [256][D]  final_layer.adaln_modulation.1.weight */
+  const void* f_modB;   /* fp16 [2D][256] final_layer.adaln_modulation.2.weight */
+  const void* f_lin;    /* fp16 [64][D]   final_layer.linear.weight */
+} hx_anima_glue_desc;
+/* Copy the glue weights (device pointers) into handle-owned memory; *gfd names them. */
+HX_API int hx_glue_load(hx_handle h, const hx_anima_glue_desc* d, int* gfd);
+/* Full sample on the blob of `meta` (Anima layout; CTX, COS and SIN filled by the caller):
+ * latent_dev fp32 [B][16][lat_h][lat_w] is denoised in place over nsteps Euler steps
+ * (nsteps <= 8). sigmas: host [nsteps + 1] or NULL for the animad schedule
+ * s = linspace(1, 0.001, nsteps), sigma = 3s / (1 + 2s), sigma_nsteps = 0 (animad.cpp:397-399).
+ * use_graph != 0 captures the whole sample once per argument set and replays it. */
+HX_API int hx_anima_sample(hx_handle h, int gfd, const int32_t* meta, int nmeta, const int* wfds, int nblk, int bfd,
+                           float* latent_dev, int lat_h, int lat_w, int nsteps, const float* sigmas, int use_graph,
+                           int32_t* rc);
+
 /* ------------------------------------------------------------------ operator level (device pointers) */
 typedef struct {
   const void* a; int lda;       /* fp16 [m][lda], columns [0,k1) */
@@ -205,6 +232,7 @@ typedef struct {
 #define HX_EPI_GELU 2
 #define HX_EPI_RMS 3
 #define HX_EPI_SITU 5
+#define HX_EPI_STORE32 6   /* fp32 output written to x / ldx */
 /* O = A W^T with a fused epilogue: gemm_run_geo (hexagon/mega/gemm2.c:96-137, moss gemm2.c:145-193). */
 HX_API int hx_gemm(hx_handle h, const hx_gemm_desc* d);
 

@@ -165,3 +165,64 @@ def pack_weights(pack, D=2048, F=8192, Cd=1024, q8=False):
         off += size
     gain = torch.from_numpy(np.frombuffer(pack[off:off + 2048], np.float32).copy())
     return W, gain
+
+
+# ---------------------------------------------------------------- per-step glue (animad.cpp:423-492)
+def sigma_schedule(steps):
+    """animad.cpp:397-399: s = linspace(1, 0.001), sigma = 3s / (1 + 2s), final 0."""
+    sig = []
+    for i in range(steps):
+        sv = 1.0 - (1.0 - 0.001) * i / (steps - 1) if steps > 1 else 1.0
+        sig.append(np.float32(3 * sv / (1 + 2 * sv)))
+    return sig + [np.float32(0.0)]
+
+
+def timestep_embedding(t, D, w_norm):
+    """animad.cpp:424-427 in float32: tp = [cos(t f_i) | sin(t f_i)], f_i = exp(-ln(1e4) i / (D/2)); emb = rms(tp) * w."""
+    half = D // 2
+    i = np.arange(half, dtype=np.float32)
+    f = np.exp(-np.log(np.float32(10000.0)) * i / np.float32(half)).astype(np.float32)
+    a = (np.float32(t) * f).astype(np.float32)
+    tp = torch.from_numpy(np.concatenate([np.cos(a), np.sin(a)]).astype(np.float32))
+    emb = tp / torch.sqrt(tp.square().mean() + 1e-6) * w_norm.float()
+    return tp, emb
+
+
+def glue_init(seed, D=2048, std=0.02):
+    g = torch.Generator().manual_seed(seed)
+    n = lambda *s: (torch.randn(*s, generator=g) * std).half()
+    return {"t_norm": (1 + torch.randn(D, generator=g) * std).half(), "t_lin1": n(D, D), "t_lin2": n(3 * D, D),
+            "x_emb": n(D, 68), "f_modA": n(256, D), "f_modB": n(2 * D, 256), "f_lin": n(64, D)}
+
+
+def patchify(lat):
+    """[B][16][H][W] -> [B][T][68] with feature c*4 + a*2 + b and a zero 17th channel (animad.cpp:447-449)."""
+    B, C, H, W = lat.shape
+    p = lat.view(B, C, H // 2, 2, W // 2, 2).permute(0, 2, 4, 1, 3, 5).reshape(B, (H // 2) * (W // 2), C * 4)
+    return torch.cat((p, torch.zeros(B, p.shape[1], 4)), -1)
+
+
+def unpatchify(y, H, W, C=16):
+    """[B][T][64] with feature (a*2+b)*16 + c -> [B][16][H][W] (animad.cpp:490-492)."""
+    B = y.shape[0]
+    return y.view(B, H // 2, W // 2, 2, 2, C).permute(0, 5, 1, 3, 2, 4).reshape(B, C, H, W)
+
+
+def sample(lat, ctx, cos, sin, blocks, glue, steps=4, sigmas=None):
+    """Full Euler sample of animad.cpp:423-492: blocks = [(W, gain, modA, modB)], glue = glue_init dict.
+    lat [B][16][H][W] fp32 -> denoised latent."""
+    sig = sigmas if sigmas is not None else sigma_schedule(steps)
+    B, C, H, Wd = lat.shape
+    D = glue["t_lin1"].shape[0]
+    lat = lat.clone()
+    for i in range(steps):
+        tp, emb = timestep_embedding(sig[i], D, glue["t_norm"])
+        lora = glue["t_lin2"].float() @ torch.nn.functional.silu(glue["t_lin1"].float() @ tp)
+        x = patchify(lat) @ glue["x_emb"].float().T
+        for (W, gain, modA, modB) in blocks:
+            x = block(x, ctx, modulation(modA, modB, emb, lora), cos, sin, W, gain)
+        fm = glue["f_modB"].float() @ (glue["f_modA"].float() @ torch.nn.functional.silu(emb)) + lora[: 2 * D]
+        h = ln_mod(x, fm[:D], fm[D:])
+        v = unpatchify(h @ glue["f_lin"].float().T, H, Wd)
+        lat = lat + (float(sig[i + 1]) - float(sig[i])) * v
+    return lat

@@ -168,3 +168,10 @@ def test_anima_pack_roundtrip():
         for n in oa.ORDER:
             err = (Wd[n] - W[n]).abs().max().item()
             assert err < (3e-3 if q8 else 1e-4), (n, err)
+
+
+def test_sigma_schedule_matches_animad():
+    sig = oa.sigma_schedule(4)
+    assert abs(float(sig[0]) - 1.0) < 1e-7 and float(sig[-1]) == 0.0
+    s = np.linspace(1, 0.001, 4)
+    np.testing.assert_allclose(np.array(sig[:4], np.float64), 3 * s / (1 + 2 * s), rtol=1e-6)
