@@ -7,6 +7,9 @@
 //  modulation: the helper-thread mat-vecs of megarun (hexagon/mega/megarun.cpp:158-171):
 //           per site h = A[256][D] silu(emb); mod = B[6144][256] h + lora.
 // One warp per row, the row held in registers (D/32 floats per lane), 16-byte loads and stores.
+#include <mutex>
+
+#include "../../include/hxdit.h"
 #include "hx_internal.h"
 #include "hx_ptx.cuh"
 
@@ -185,3 +188,42 @@ cudaError_t f32_to_f16_launch(const float* src, __half* dst, size_t n, cudaStrea
 }
 
 }  // namespace hx
+
+// ---------------------------------------------------------------- allocation-free modulation
+// Scratch of hx_modulation_noalloc: the per-site 256-wide hidden vectors (stage 1 output, stage 2
+// input). Fixed at 4096 floats; every GPU that loads the library holds it until the process exits.
+#define HX_NOALLOC_MOD_HID_FLOATS 4096
+static __device__ __align__(256) float g_noalloc_mod_hid[HX_NOALLOC_MOD_HID_FLOATS];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_hid_ptr[64];  // device address of g_noalloc_mod_hid per device, looked up once
+}  // namespace
+
+extern "C" HX_API int hx_modulation_noalloc(const void* modA, const void* modB, const float* emb_dev,
+                                            const float* lora_dev, float* mod_dev, int nsite, int D, void* stream) {
+  if (!modA || !modB || !emb_dev || !mod_dev || nsite <= 0 || D <= 0 || D % 256) return HX_E_ARG;
+  if (static_cast<long>(nsite) * 256 > HX_NOALLOC_MOD_HID_FLOATS) return HX_E_SCRATCH;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_E_CUDA;
+  void* hid = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_hid_ptr[dev]) {
+      // In host code g_noalloc_mod_hid only stands for the symbol: its device address comes from here.
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_mod_hid) != cudaSuccess || !p) return HX_E_CUDA;
+      g_noalloc_hid_ptr[dev] = p;
+    }
+    hid = g_noalloc_hid_ptr[dev];
+  }
+  // Stage 1 writes every hid element stage 2 reads, so nothing needs clearing between calls.
+  const int R = 256, O = 3 * D, t = 256, wpb = t / 32;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  hx::mod_stage1<<<(nsite * R + wpb - 1) / wpb, t, 0, s>>>(static_cast<const __half*>(modA), emb_dev,
+                                                            static_cast<float*>(hid), nsite, D, R);
+  hx::mod_stage2<<<(nsite * O + wpb - 1) / wpb, t, 0, s>>>(static_cast<const __half*>(modB),
+                                                            static_cast<const float*>(hid), lora_dev, mod_dev, nsite,
+                                                            R, O);
+  return cudaGetLastError() == cudaSuccess ? HX_OK : HX_E_CUDA;
+}

@@ -19,8 +19,9 @@ LIB_PATH = os.path.join(_HERE, "libhxdit.so")
 
 HX_OK = 0
 HX_E_ARG, HX_E_CUDA, HX_E_NOWEIGHTS, HX_E_NOBLOB, HX_E_RANGE, HX_E_FORMAT, HX_E_TIMEOUT = -1, -2, -5, -6, -7, -8, -77
+HX_E_SCRATCH = -9
 ERRORS = {-1: "HX_E_ARG", -2: "HX_E_CUDA", -5: "HX_E_NOWEIGHTS", -6: "HX_E_NOBLOB", -7: "HX_E_RANGE",
-          -8: "HX_E_FORMAT", -77: "HX_E_TIMEOUT"}
+          -8: "HX_E_FORMAT", -9: "HX_E_SCRATCH", -77: "HX_E_TIMEOUT"}
 
 MODEL_ANIMA, MODEL_MOSS = 1, 2
 FMT_F16, FMT_Q8, FMT_Q4A, FMT_Q4 = 0, 1, 2, 3
@@ -116,6 +117,7 @@ _SIGS = {
     "hx_blob_layout": [_i, _i, _i, _i, _i, _i, _i, _ip, _i, ctypes.POINTER(_sz)],
     "hx_mega_block": [_vp, _ip, _i, _i, _i, _vp, _i, _ip, _i, _ip],
     "hx_modulation": [_vp, _i, _vp, _vp, _vp],
+    "hx_modulation_noalloc": [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "hx_chain": [_vp, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _vp, _vp, ctypes.c_uint32, _i, _ip],
     "hx_glue_load": [_vp, ctypes.POINTER(hx_anima_glue_desc), ctypes.POINTER(_i)],
     "hx_anima_sample": [_vp, _i, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _i, _i, _i, _vp, _i, _ip],
@@ -177,6 +179,13 @@ def rope_moss(H, W, T, bands, ntok=None):
     s = np.zeros((ntok, 64), np.float32)
     _check(lib().hx_rope_moss(H, W, T, b.ctypes.data, ntok, c.ctypes.data, s.ctypes.data), "hx_rope_moss")
     return c, s
+
+
+def modulation_noalloc(modA, modB, emb, lora, mod_out, nsite, D, stream=None):
+    """hx_modulation_noalloc: the per-site AdaLN modulation without a handle and without allocating;
+    for callers that cannot call cudaMalloc (see include/hxdit.h). Scratch is a fixed static device array."""
+    _check(lib().hx_modulation_noalloc(_ptr(modA), _ptr(modB), _ptr(emb), _ptr(lora), _ptr(mod_out), nsite, D, stream),
+           "hx_modulation_noalloc")
 
 
 def make_mat(fmt, n, k, w, scale=None, minv=None, group=None):

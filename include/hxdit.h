@@ -41,6 +41,7 @@ extern "C" {
 #define HX_E_RANGE (-7)     /* meta offsets reach outside the blob (reference: -7 blob map) */
 #define HX_E_FORMAT (-8)    /* pack bytes do not match a known pack layout */
 #define HX_E_TIMEOUT (-77)  /* a device-side bounded wait expired (reference: -77 HMX self-test) */
+#define HX_E_SCRATCH (-9)   /* request larger than a fixed static scratch area (hx_modulation_noalloc) */
 
 /* ------------------------------------------------------------------ models and weight formats */
 #define HX_MODEL_ANIMA 1    /* hexagon/mega: D 2048, 16 heads, self + cross attention, GELU MLP */
@@ -175,6 +176,21 @@ HX_API int hx_mega_block(hx_handle h, const int32_t* meta, int nmeta, int wfd, i
  * for site s: mod[3s..3s+2][D] = B_s (A_s silu(emb)) + lora[0:3D]. emb [D], lora [3D], mod [9D]
  * device fp32; mod_dev must hold 9*D + 3*256 floats (the tail is scratch). */
 HX_API int hx_modulation(hx_handle h, int wfd, const float* emb_dev, const float* lora_dev, float* mod_dev);
+
+/* Allocation-free variant of hx_modulation, with no counterpart in the reference. For callers that
+ * cannot call cudaMalloc: code that runs while another thread captures a CUDA graph in the global
+ * capture mode, hosts that run from a fixed, pre-reserved memory pool (as the reference's DSP side runs
+ * from a fixed VTCM/rpcmem region), or callers that never open a handle because hx_open allocates.
+ * It needs no handle: modA [nsite][256][D] and modB [nsite][3D][256] are fp16 device arrays, emb [D],
+ * lora [3D] (may be NULL) and mod [nsite][3D] fp32 device arrays, stream a cudaStream_t (NULL = the
+ * legacy default stream) of the current device. The 256-wide hidden vectors live in a static device
+ * array of 4096 floats (16 KB) that every GPU loading the library holds until the process exits, so
+ * nsite * 256 must be <= 4096 (else HX_E_SCRATCH). The first call on a device looks up that array's
+ * device address with the device current; make that first call before any stream capture. All calls
+ * share the array and each call overwrites the part it reads before reading it; calls whose kernels
+ * overlap on the GPU (different streams without ordering) race on it. Allocates nothing. */
+HX_API int hx_modulation_noalloc(const void* modA, const void* modB, const float* emb_dev, const float* lora_dev,
+                                 float* mod_dev, int nsite, int D, void* stream);
 
 /* Run `count` blocks in order on one blob: the megarun chain (megarun.cpp:176-184).
  * Anima: mods_dev NULL -> each block's modulation is computed from emb_dev/lora_dev first;
