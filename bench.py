@@ -102,6 +102,13 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def images_per_rank(batch, world):
+    """Image-batch data parallelism: every rank denoises batch / world whole images."""
+    if world <= 0 or batch % world:
+        raise ValueError(f"batch {batch} does not split over {world} ranks")
+    return batch // world
+
+
 # ---------------------------------------------------------------------------------------- CPU legs
 def cpu_block_seconds(reps=2, threads=None):
     """Oracle Anima block (torch fp32) at the config shape, one image: seconds per block (median)."""
@@ -221,9 +228,7 @@ def run_ours(args, rank, world, local_rank):
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
-    if args.batch % world:
-        raise SystemExit(f"batch {args.batch} does not split over {world} ranks")
-    B = args.batch // world
+    B = images_per_rank(args.batch, world)
     h = rt.Handle(local_rank)
     stream = torch.cuda.ExternalStream(h.stream())
     wfds, keep = synth_weights(h, rt, torch, dev, 1234)

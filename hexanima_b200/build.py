@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libhxdit.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-SOURCES = ["gemm.cu", "attn.cu", "elem.cu", "repack.cu", "glue.cu", "api.cpp"]
+SOURCES = ["gemm.cu", "attn.cu", "elem.cu", "repack.cu", "glue.cu", "sp.cu", "api.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I" + os.path.join(ROOT, "include")]
 
@@ -56,11 +56,29 @@ def build(force=False, jobs=None, verbose=False):
     with ThreadPoolExecutor(max_workers=jobs or len(SOURCES)) as ex:
         objs = list(ex.map(lambda s: _compile(s, force, headers, verbose), SOURCES))
     if force or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs
+        cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", LIB] + objs + ["-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    _build_hxrun(force)
     return LIB
+
+
+HXRUN = os.path.join(HERE, "hxrun")
+
+
+def _build_hxrun(force=False):
+    """The megarun-protocol CLI, linked against the in-tree libhxdit.so (rpath $ORIGIN)."""
+    src = os.path.join(CSRC, "hxrun.cpp")
+    if not force and os.path.exists(HXRUN) and os.path.getmtime(HXRUN) >= max(
+            os.path.getmtime(src), os.path.getmtime(LIB), os.path.getmtime(os.path.join(ROOT, "include", "hxdit.h"))):
+        return HXRUN
+    cmd = ["g++", "-O2", "-std=c++17", "-I" + os.path.join(ROOT, "include"), src, "-L" + HERE, "-lhxdit",
+           "-Wl,-rpath,$ORIGIN", "-o", HXRUN]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"hxrun build failed:\n{r.stdout}\n{r.stderr}")
+    return HXRUN
 
 
 if __name__ == "__main__":

@@ -23,6 +23,7 @@
 
 #include "../../include/hxdit.h"
 #include "hx_internal.h"
+#include "hx_sp.h"
 
 using namespace hx;
 
@@ -94,6 +95,7 @@ struct hx_ctx {
   uint64_t graph_clock = 0;
   std::map<int, std::unique_ptr<Glue>> glues;
   SampleScratch ss;
+  hx::SpState sp;
   std::mutex mu;
   void drop_graphs() {
     for (auto& g : graphs)
@@ -421,7 +423,7 @@ int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob,
 int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, const float* mod, Stage& st) {
   const int D = W.D, F = W.F, H = W.H;
   const int T = meta[HX_S_NTOK];
-  const int nvalid = meta[HX_S_NVALID] > 0 ? meta[HX_S_NVALID] : T;
+  const int nvalid = meta[HX_S_NVALID] > 0 ? meta[HX_S_NVALID] : T * (meta[HX_S_SP] > 1 ? meta[HX_S_SP] : 1);
   const int B = meta[HX_S_BATCH] > 0 ? meta[HX_S_BATCH] : 1;
   if (meta[HX_S_MODE] != 0) return HX_E_ARG;  // text-refiner / projection modes are not built
   const int rows = B * T;
@@ -486,14 +488,19 @@ int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, 
     CKL(gemm_launch(g, s));
   }
   if (st.tick()) return HX_OK;
-  AttnArgs a;
-  a.q = qkv; a.ldq = 3 * D; a.q_col0 = 0;
-  a.k = qkv; a.ldk = 3 * D; a.k_col0 = D;
-  a.v = qkv; a.ldv = 3 * D; a.v_col0 = 2 * D;
-  a.o = obuf; a.ldo = D;
-  a.B = B; a.H = H; a.Tq = T; a.Tk = T; a.nvalid = nvalid;
-  a.status = h->status;
-  CKL(attn_launch(a, s));
+  const int sp = meta[HX_S_SP];
+  if (sp > 1) {  // Ulysses: token shards -> head shards -> full-sequence attention -> back
+    CKL(hx::sp_attention(h->sp, qkv, obuf, D, T, D, H, nvalid, h->status, s));
+  } else {
+    AttnArgs a;
+    a.q = qkv; a.ldq = 3 * D; a.q_col0 = 0;
+    a.k = qkv; a.ldk = 3 * D; a.k_col0 = D;
+    a.v = qkv; a.ldv = 3 * D; a.v_col0 = 2 * D;
+    a.o = obuf; a.ldo = D;
+    a.B = B; a.H = H; a.Tq = T; a.Tk = T; a.nvalid = nvalid;
+    a.status = h->status;
+    CKL(attn_launch(a, s));
+  }
   if (st.tick()) return HX_OK;
   {
     if (lora) {
@@ -579,7 +586,9 @@ int check_meta(const Weights& W, const int32_t* meta, int nmeta, size_t blob_byt
     const size_t T = meta[HX_S_NTOK];
     const size_t B = (nmeta > HX_S_BATCH && meta[HX_S_BATCH] > 0) ? meta[HX_S_BATCH] : 1;
     if (T == 0 || T % 32) return HX_E_ARG;
-    if (meta[HX_S_NVALID] < 0 || static_cast<size_t>(meta[HX_S_NVALID]) > T) return HX_E_ARG;
+    const int sp = nmeta > HX_S_SP ? meta[HX_S_SP] : 0;
+    if (sp > 1 && B != 1) return HX_E_ARG;
+    if (meta[HX_S_NVALID] < 0 || static_cast<size_t>(meta[HX_S_NVALID]) > T * (sp > 1 ? sp : 1)) return HX_E_ARG;
     const size_t D = W.D, F = W.F, R = B * T;
     if (!in(meta[HX_S_X], R * D * 4) || !in(meta[HX_S_COS], T * 256) || !in(meta[HX_S_SIN], T * 256) ||
         !in(meta[HX_S_H], R * D * 2) || !in(meta[HX_S_Q], R * 3 * D * 2) || !in(meta[HX_S_O], R * D * 2) ||
@@ -710,7 +719,8 @@ int hx_close(hx_handle hh) {
   {
     DevGuard g(h->device);
     cudaStreamSynchronize(h->stream);
-    h->drop_graphs();
+    h->drop_graphs();  // graphs holding NCCL calls go before the communicator
+    hx::sp_comm_destroy(h->sp);
     for (auto& kv : h->bufs) cudaFree(kv.second.ptr);
     for (auto& kv : h->weights)
       for (void* p : kv.second->owned) cudaFree(p);
@@ -994,6 +1004,10 @@ int hx_mega_block(hx_handle hh, const int32_t* meta, int nmeta, int wfd, int bfd
     if (cudaMemcpyAsync(mod_dev, mod, static_cast<size_t>(nmod) * 4, cudaMemcpyHostToDevice, h->stream) != cudaSuccess)
       return (*rc = HX_E_CUDA);
   }
+  if (!anima && m[HX_S_SP] > 1) {
+    if (!h->sp.comm || h->sp.nranks != m[HX_S_SP]) return (*rc = HX_E_ARG);
+    if (hx::sp_reserve(h->sp, m[HX_S_NTOK], D)) return (*rc = HX_E_CUDA);
+  }
   Stage st{h, times ? ntimes : 0, 0, anima ? m[HX_A_STOP] : m[HX_S_STOP]};
   if (st.ntimes > 0) cudaEventRecord(h->ev[0], h->stream);
   if (times && ntimes > 24)
@@ -1017,6 +1031,17 @@ int hx_mega_block(hx_handle hh, const int32_t* meta, int nmeta, int wfd, int bfd
   }
   if (cudaPeekAtLastError() != cudaSuccess) return (*rc = HX_E_CUDA);
   return HX_OK;
+}
+
+int hx_sp_unique_id(void* id128) { return hx::sp_unique_id(id128) == 0 ? HX_OK : HX_E_CUDA; }
+
+int hx_sp_init(hx_handle hh, int nranks, int rank, const void* id128) {
+  hx_ctx* h = H(hh);
+  if (!h || !id128 || nranks < 2 || rank < 0 || rank >= nranks) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  if (h->sp.comm) return HX_E_ARG;
+  DevGuard g(h->device);
+  return hx::sp_comm_init(h->sp, nranks, rank, id128) == 0 ? HX_OK : HX_E_CUDA;
 }
 
 int hx_modulation(hx_handle hh, int wfd, const float* emb_dev, const float* lora_dev, float* mod_dev) {
@@ -1058,6 +1083,10 @@ int hx_chain(hx_handle hh, const int32_t* meta, int nmeta, const int* wfds, int 
   DevGuard g(h->device);
   if (!mods_dev)
     if (int r = ensure_modscratch(h, kModStride(D) * count)) return (*rc = r);
+  if (model == HX_MODEL_MOSS && m[HX_S_SP] > 1) {
+    if (!h->sp.comm || h->sp.nranks != m[HX_S_SP]) return (*rc = HX_E_ARG);
+    if (hx::sp_reserve(h->sp, m[HX_S_NTOK], D)) return (*rc = HX_E_CUDA);
+  }
   uint8_t* blob = static_cast<uint8_t*>(bi->second.ptr);
   std::vector<int64_t> key(m.begin(), m.end());
   for (int k = 0; k < count; ++k) key.push_back(wfds[k]);
@@ -1249,6 +1278,7 @@ int hx_gemm(hx_handle hh, const hx_gemm_desc* d) {
   a.cosT = d->cos_t;
   a.sinT = d->sin_t;
   a.eps = d->eps > 0.f ? d->eps : 1e-6f;
+  a.tile = d->tile;
   a.status = h->status;
   cudaError_t e = gemm_launch(a, h->stream);
   return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);

@@ -58,6 +58,7 @@ struct GemmArgs {
   float eps = 1e-6f;
   int* status = nullptr;
   int max_ctas = 0;  // 0 = one CTA per SM
+  int tile = 0;      // 0 auto, 1 single-CTA 128x256 tiles, 2 CTA-pair 256x256 tiles
 };
 
 struct AttnArgs {

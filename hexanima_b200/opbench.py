@@ -25,6 +25,7 @@ def main(argv=None):
     ap.add_argument("--ops", default="all")
     ap.add_argument("--fmt", choices=["q8", "f16", "q4"], default="q8")
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--tile", type=int, default=0, help="GEMM tiles: 0 auto, 1 single-CTA, 2 CTA pair")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     h = rt.Handle(0)
@@ -81,24 +82,24 @@ def main(argv=None):
     ops = {}
     mq, mo, m1, m2 = mat(3 * D, D), mat(D, D), mat(F if a.model == "anima" else 2 * F, D), mat(D, F)
     ops["qkv"] = (lambda: h.gemm(A, M, mq, rt.EPI_RMS, lda=D, out=qkv, ldo=3 * D, gain0=gain, gain1=gain, seg1=D,
-                                 seg2=2 * D, rope0=1, rope1=1, cos_t=cos, sin_t=sin, rows_per_img=T),
+                                 seg2=2 * D, rope0=1, rope1=1, cos_t=cos, sin_t=sin, rows_per_img=T, tile=a.tile),
                   2.0 * M * 3 * D * D, "TFLOP/s")
-    ops["o"] = (lambda: h.gemm(A, M, mo, rt.EPI_RESID, lda=D, x=x, ldx=D, gate=gate), 2.0 * M * D * D, "TFLOP/s")
+    ops["o"] = (lambda: h.gemm(A, M, mo, rt.EPI_RESID, lda=D, x=x, ldx=D, gate=gate, tile=a.tile), 2.0 * M * D * D, "TFLOP/s")
     if a.model == "anima":
         ctx = torch.randn(B * C, CD, device=dev, generator=g).half()
         ckvb = torch.empty(B * C, 2 * D, device=dev).half()
         mckv = mat(2 * D, CD)
         ops["ckv"] = (lambda: h.gemm(ctx, B * C, mckv, rt.EPI_RMS, lda=CD, out=ckvb, ldo=2 * D, gain0=gain, seg1=D,
-                                     seg2=D), 2.0 * B * C * 2 * D * CD, "TFLOP/s")
-        ops["m1"] = (lambda: h.gemm(A, M, m1, rt.EPI_GELU, lda=D, out=mid, ldo=F), 2.0 * M * F * D, "TFLOP/s")
+                                     seg2=D, tile=a.tile), 2.0 * B * C * 2 * D * CD, "TFLOP/s")
+        ops["m1"] = (lambda: h.gemm(A, M, m1, rt.EPI_GELU, lda=D, out=mid, ldo=F, tile=a.tile), 2.0 * M * F * D, "TFLOP/s")
         ops["cross_attn"] = (lambda: h.attention(qkv, ckvb, ckvb, o, B, H, T, C, 3 * D, 2 * D, 2 * D, D, 0, 0, D),
                              4.0 * B * T * C * D, "TFLOP/s")
         ops["lnmod"] = (lambda: h.lnmod(x, A, M, D, sh, sc), 6.0 * M * D, "GB/s")
     else:
-        ops["m1"] = (lambda: h.gemm(A, M, m1, rt.EPI_SITU, lda=D, out=mid, ldo=F), 2.0 * M * 2 * F * D, "TFLOP/s")
+        ops["m1"] = (lambda: h.gemm(A, M, m1, rt.EPI_SITU, lda=D, out=mid, ldo=F, tile=a.tile), 2.0 * M * 2 * F * D, "TFLOP/s")
         wn = torch.ones(D, device=dev)
         ops["rmsmod"] = (lambda: h.rmsmod(x, A, M, D, wn, sh, sc), 6.0 * M * D, "GB/s")
-    ops["m2"] = (lambda: h.gemm(Amid, M, m2, rt.EPI_RESID, lda=F, x=x, ldx=D, gate=gate), 2.0 * M * F * D, "TFLOP/s")
+    ops["m2"] = (lambda: h.gemm(Amid, M, m2, rt.EPI_RESID, lda=F, x=x, ldx=D, gate=gate, tile=a.tile), 2.0 * M * F * D, "TFLOP/s")
     ops["self_attn"] = (lambda: h.attention(qkv, qkv, qkv, o, B, H, T, T, 3 * D, 3 * D, 3 * D, D, 0, D, 2 * D),
                         4.0 * B * T * T * D, "TFLOP/s")
     names = list(ops) if a.ops == "all" else a.ops.split(",")

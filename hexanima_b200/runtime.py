@@ -41,7 +41,8 @@ S_SLOTS = ["X", "COS", "SIN", "H", "Q", "K", "V", "O", "T", "MID", "LQ", "LO", "
 S = {n: i for i, n in enumerate(S_SLOTS)}
 S["NMETA"] = 26
 S["BATCH"] = 26
-S_NMETA_EXT = 27
+S["SP"] = 27
+S_NMETA_EXT = 28
 
 
 class HxError(RuntimeError):
@@ -84,7 +85,8 @@ class hx_gemm_desc(ctypes.Structure):
                 ("gate", ctypes.c_void_p), ("vec_bstride", ctypes.c_long), ("rows_per_img", ctypes.c_int),
                 ("gain0", ctypes.c_void_p), ("gain1", ctypes.c_void_p), ("seg1", ctypes.c_int),
                 ("seg2", ctypes.c_int), ("rope0", ctypes.c_int), ("rope1", ctypes.c_int),
-                ("cos_t", ctypes.c_void_p), ("sin_t", ctypes.c_void_p), ("eps", ctypes.c_float)]
+                ("cos_t", ctypes.c_void_p), ("sin_t", ctypes.c_void_p), ("eps", ctypes.c_float),
+                ("tile", ctypes.c_int)]
 
 
 class hx_attn_desc(ctypes.Structure):
@@ -116,6 +118,8 @@ _SIGS = {
     "hx_weights_free": [_vp, _i],
     "hx_blob_layout": [_i, _i, _i, _i, _i, _i, _i, _ip, _i, ctypes.POINTER(_sz)],
     "hx_mega_block": [_vp, _ip, _i, _i, _i, _vp, _i, _ip, _i, _ip],
+    "hx_sp_unique_id": [_vp],
+    "hx_sp_init": [_vp, _i, _i, _vp],
     "hx_modulation": [_vp, _i, _vp, _vp, _vp],
     "hx_modulation_noalloc": [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "hx_chain": [_vp, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _vp, _vp, ctypes.c_uint32, _i, _ip],
@@ -186,6 +190,13 @@ def modulation_noalloc(modA, modB, emb, lora, mod_out, nsite, D, stream=None):
     for callers that cannot call cudaMalloc (see include/hxdit.h). Scratch is a fixed static device array."""
     _check(lib().hx_modulation_noalloc(_ptr(modA), _ptr(modB), _ptr(emb), _ptr(lora), _ptr(mod_out), nsite, D, stream),
            "hx_modulation_noalloc")
+
+
+def sp_unique_id():
+    """128-byte id for hx_sp_init (create on one rank, share with all)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(lib().hx_sp_unique_id(buf), "hx_sp_unique_id")
+    return buf.raw
 
 
 def make_mat(fmt, n, k, w, scale=None, minv=None, group=None):
@@ -272,6 +283,10 @@ class Handle:
         self._keep.append(keep)  # the caller's device arrays must outlive the binding
         return wfd.value
 
+    def sp_init(self, nranks, rank, id128):
+        buf = ctypes.create_string_buffer(bytes(id128), 128)
+        _check(lib().hx_sp_init(self.h, nranks, rank, buf), "hx_sp_init")
+
     def weights_free(self, wfd):
         _check(lib().hx_weights_free(self.h, wfd), "hx_weights_free")
 
@@ -326,10 +341,10 @@ class Handle:
     # -------------------------------------------------------------- operators
     def gemm(self, a, m, mat, epi=EPI_STORE, lda=None, k1=0, a2=None, lda2=0, out=None, ldo=0, x=None, ldx=0,
              gate=None, vec_bstride=0, rows_per_img=0, gain0=None, gain1=None, seg1=0, seg2=0, rope0=0, rope1=0,
-             cos_t=None, sin_t=None, eps=1e-6):
+             cos_t=None, sin_t=None, eps=1e-6, tile=0):
         d = hx_gemm_desc(_ptr(a), lda if lda is not None else mat.k, _ptr(a2), lda2, m, k1, mat, epi, _ptr(out), ldo,
                          _ptr(x), ldx, _ptr(gate), vec_bstride, rows_per_img, _ptr(gain0), _ptr(gain1), seg1, seg2,
-                         rope0, rope1, _ptr(cos_t), _ptr(sin_t), eps)
+                         rope0, rope1, _ptr(cos_t), _ptr(sin_t), eps, tile)
         _check(lib().hx_gemm(self.h, ctypes.byref(d)), "hx_gemm")
 
     def attention(self, q, k, v, o, batch, heads, tq, tk, ldq, ldk, ldv, ldo, q_col0=0, k_col0=0, v_col0=0,

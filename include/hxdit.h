@@ -156,6 +156,9 @@ enum {
   HX_S_FIRST, HX_S_MODE, HX_S_NCB, HX_S_FMT, HX_S_ROWS, HX_S_CS, HX_S_WOFF,
   HX_S_NMETA,               /* 26, the reference's M_NMETA */
   HX_S_BATCH = HX_S_NMETA,  /* extension: images stacked in the blob (default 1) */
+  HX_S_SP,                  /* extension: P > 1 runs the attention sequence-parallel over the handle's
+                               communicator (hx_sp_init): NTOK is this rank's token count, NVALID the
+                               image's valid token count over all P shards; batch must be 1 */
   HX_S_NMETA_EXT
 };
 
@@ -164,6 +167,14 @@ enum {
  * the mod vectors go to the CS slot. */
 HX_API int hx_blob_layout(int model, int ntok, int nctx, int batch, int D, int F, int Cd, int32_t* meta, int nmeta,
                    size_t* total);
+
+/* Ulysses sequence parallelism across GPUs (no counterpart in the single-device reference):
+ * rank 0 creates a 128-byte id with hx_sp_unique_id and every rank passes it to hx_sp_init (a
+ * collective over the P ranks). MOSS blocks with meta[HX_S_SP] = P then exchange q|k|v token shards
+ * for head shards (NCCL grouped send/recv), attend over the full sequence on H/P heads and exchange
+ * the outputs back. The communicator lives until hx_close. */
+HX_API int hx_sp_unique_id(void* id128);
+HX_API int hx_sp_init(hx_handle h, int nranks, int rank, const void* id128);
 
 /* One DiT block forward: mega_block (hexagon/mega/mega.idl:10). mod: host fp32 modulation
  * (Anima 9*D floats, MOSS 6*D; modlen in bytes) copied per call, or NULL to read it from the blob.
@@ -242,6 +253,7 @@ typedef struct {
   int seg1, seg2, rope0, rope1;
   const float* cos_t; const float* sin_t;   /* [rows_per_img][64] */
   float eps;
+  int tile;                     /* 0 auto, 1 single-CTA 128x256 tiles, 2 CTA-pair 256x256 tiles */
 } hx_gemm_desc;
 #define HX_EPI_STORE 0
 #define HX_EPI_RESID 1

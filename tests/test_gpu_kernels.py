@@ -24,27 +24,31 @@ def h():
     hd.close()
 
 
-def _onehot_dequant(h, fmt, w, group):
+TILES = [1, 2]  # single-CTA 128x256 tiles, CTA-pair 256x256 tiles (cta_group::2)
+
+
+def _onehot_dequant(h, fmt, w, group, tile):
     """out = I * W^T reproduces the device's dequantised operand exactly (one fp32 product per output)."""
     N, K = w.shape
     mat, keep, deq = make_mat(fmt, w, group)
     A = torch.eye(K, dtype=torch.float16, device="cuda")
     out = torch.zeros(K, N, dtype=torch.float16, device="cuda")
-    h.gemm(A, K, mat, rt.EPI_STORE, lda=K, out=out, ldo=N)
+    h.gemm(A, K, mat, rt.EPI_STORE, lda=K, out=out, ldo=N, tile=tile)
     h.sync()
     return out.cpu().T.contiguous(), deq
 
 
+@pytest.mark.parametrize("tile", TILES)
 @pytest.mark.parametrize("fmt,group", [(rt.FMT_F16, 64), (rt.FMT_Q8, 32), (rt.FMT_Q8, 64), (rt.FMT_Q4, 32),
                                        (rt.FMT_Q4A, 32)])
-def test_dequant_bit_exact(h, fmt, group):
+def test_dequant_bit_exact(h, fmt, group, tile):
     rng = np.random.default_rng(7)
     N, K = 320, 256
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     w[3] *= 1e-3     # small scales: subnormal fp16 products
     w[7] *= 300.0    # large values
     w[11] = 0.0
-    got, deq = _onehot_dequant(h, fmt, w, group)
+    got, deq = _onehot_dequant(h, fmt, w, group, tile)
     ref = deq.half()
     assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), int((got != ref).sum())
 
@@ -53,8 +57,9 @@ def _ref_gemm(A16, Wd):
     return A16.float().cpu() @ Wd.T
 
 
+@pytest.mark.parametrize("tile", TILES)
 @pytest.mark.parametrize("fmt", [rt.FMT_F16, rt.FMT_Q8, rt.FMT_Q4])
-def test_gemm_store_and_gelu(h, fmt):
+def test_gemm_store_and_gelu(h, fmt, tile):
     torch.manual_seed(1)
     M, K, N = 300, 512, 544
     A = torch.randn(M, K).half()
@@ -62,12 +67,13 @@ def test_gemm_store_and_gelu(h, fmt):
     ref = _ref_gemm(A, Wd)
     for epi, f in ((rt.EPI_STORE, lambda t: t), (rt.EPI_GELU, oa.gelu)):
         out = torch.zeros(M, N, dtype=torch.float16, device="cuda")
-        h.gemm(A.cuda(), M, mat, epi, lda=K, out=out, ldo=N)
+        h.gemm(A.cuda(), M, mat, epi, lda=K, out=out, ldo=N, tile=tile)
         h.sync()
         assert rel(out.float(), f(ref)) < 2e-3
 
 
-def test_gemm_large_k_and_lora_a2(h):
+@pytest.mark.parametrize("tile", TILES)
+def test_gemm_large_k_and_lora_a2(h, tile):
     torch.manual_seed(2)
     M, K1, N = 256, 8192, 512
     A = torch.randn(M, K1).half() * 0.5
@@ -77,13 +83,15 @@ def test_gemm_large_k_and_lora_a2(h):
     out = torch.zeros(M, N, dtype=torch.float16, device="cuda")
     Lc = L.cuda()
     # extra K columns come from columns 128..255 of L (the k slice of the fused LoRA-A output)
-    h.gemm(A.cuda(), M, mat, rt.EPI_STORE, lda=K1, k1=K1, a2=Lc.data_ptr() + 128 * 2, lda2=384, out=out, ldo=N)
+    h.gemm(A.cuda(), M, mat, rt.EPI_STORE, lda=K1, k1=K1, a2=Lc.data_ptr() + 128 * 2, lda2=384, out=out, ldo=N,
+           tile=tile)
     h.sync()
     ref = torch.cat((A.float(), L[:, 128:256].float()), 1) @ Wd.T
     assert rel(out.float(), ref) < 2e-3
 
 
-def test_gemm_residual(h):
+@pytest.mark.parametrize("tile", TILES)
+def test_gemm_residual(h, tile):
     torch.manual_seed(3)
     B, T, K, N = 2, 160, 256, 512
     M = B * T
@@ -93,13 +101,14 @@ def test_gemm_residual(h):
     gate = torch.randn(B, N)
     x = x0.cuda()
     g = gate.cuda()
-    h.gemm(A.cuda(), M, mat, rt.EPI_RESID, lda=K, x=x, ldx=N, gate=g, vec_bstride=N, rows_per_img=T)
+    h.gemm(A.cuda(), M, mat, rt.EPI_RESID, lda=K, x=x, ldx=N, gate=g, vec_bstride=N, rows_per_img=T, tile=tile)
     h.sync()
     ref = x0 + gate.repeat_interleave(T, 0) * _ref_gemm(A, Wd)
     assert rel(x.cpu() - x0, ref - x0) < 2e-3
 
 
-def test_gemm_rms_rope_segments(h):
+@pytest.mark.parametrize("tile", TILES)
+def test_gemm_rms_rope_segments(h, tile):
     torch.manual_seed(4)
     T, K, D = 192, 256, 256  # 2 heads per segment; q | k | v = 768 columns
     A = torch.randn(T, K).half()
@@ -110,7 +119,7 @@ def test_gemm_rms_rope_segments(h):
     out = torch.zeros(T, 3 * D, dtype=torch.float16, device="cuda")
     gqc, gkc, cc, sc = gq.cuda(), gk.cuda(), cos.cuda(), sin.cuda()
     h.gemm(A.cuda(), T, mat, rt.EPI_RMS, lda=K, out=out, ldo=3 * D, gain0=gqc, gain1=gkc, seg1=D, seg2=2 * D,
-           rope0=1, rope1=1, cos_t=cc, sin_t=sc, rows_per_img=T)
+           rope0=1, rope1=1, cos_t=cc, sin_t=sc, rows_per_img=T, tile=tile)
     h.sync()
     ref = _ref_gemm(A, Wd)
     H = D // 128
@@ -120,7 +129,8 @@ def test_gemm_rms_rope_segments(h):
     assert rel(o[:, :D], q) < 2e-3 and rel(o[:, D:2 * D], k) < 2e-3 and rel(o[:, 2 * D:], ref[:, 2 * D:]) < 2e-3
 
 
-def test_gemm_situ(h):
+@pytest.mark.parametrize("tile", TILES)
+def test_gemm_situ(h, tile):
     torch.manual_seed(5)
     M, K, F = 200, 256, 512
     A = torch.randn(M, K).half()
@@ -129,11 +139,28 @@ def test_gemm_situ(h):
     w = op.situ_rows(up.numpy(), gate.numpy())
     mat, keep, Wd = make_mat(rt.FMT_Q8, w, 32)
     out = torch.zeros(M, F, dtype=torch.float16, device="cuda")
-    h.gemm(A.cuda(), M, mat, rt.EPI_SITU, lda=K, out=out, ldo=F)
+    h.gemm(A.cuda(), M, mat, rt.EPI_SITU, lda=K, out=out, ldo=F, tile=tile)
     h.sync()
     ug = _ref_gemm(A, Wd).view(M, F // 128, 2, 128)
     ref = om.situ(ug[:, :, 0], ug[:, :, 1]).reshape(M, F)
     assert rel(out.float(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("fmt", [rt.FMT_F16, rt.FMT_Q8, rt.FMT_Q4A])
+def test_gemm_pair_tiles_large(h, fmt):
+    """A shape where the automatic choice takes CTA pairs (many 256x256 tiles) against the single-CTA result."""
+    torch.manual_seed(9)
+    M, K, N = 4096, 1024, 2048
+    A = torch.randn(M, K, device="cuda").half()
+    mat, keep, Wd = make_mat(fmt, (torch.randn(N, K) * 0.05).numpy(), 32)
+    o1 = torch.zeros(M, N, dtype=torch.float16, device="cuda")
+    o2 = torch.zeros(M, N, dtype=torch.float16, device="cuda")
+    h.gemm(A, M, mat, rt.EPI_GELU, lda=K, out=o1, ldo=N, tile=1)
+    h.gemm(A, M, mat, rt.EPI_GELU, lda=K, out=o2, ldo=N, tile=0)
+    h.sync()
+    ref = oa.gelu(A.float().cpu() @ Wd.T)
+    assert rel(o1.float(), ref) < 2e-3 and rel(o2.float(), ref) < 2e-3
+    assert rel(o1.float(), o2.float()) < 1e-3
 
 
 @pytest.mark.parametrize("B,H,Tq,Tk,nvalid", [(2, 2, 200, 333, 300), (1, 3, 256, 256, 0), (2, 16, 1536, 1536, 0),
