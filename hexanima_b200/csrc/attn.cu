@@ -34,6 +34,13 @@ constexpr int TILE_BYTES = 128 * 128 * 2;  // 32 KB: two 64-column swizzled halv
 constexpr int SMEM_Q = 0, SMEM_KV = TILE_BYTES, SMEM_P = TILE_BYTES * 5;
 constexpr int ATT_SMEM = TILE_BYTES * 6 + 1024 + 1024;
 
+// one MUFU op: 2^x (flush-to-zero; the inputs here are <= 0 and the results feed fp16 probabilities)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct AParams {
   int Tq, Tk, nvalid, H, nkt;
   float scale_log2;
@@ -196,23 +203,33 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const uint32_t ts = tmem + tl + sb * 128;
       const int key0 = j * KT;
       const bool full_tile = key0 + KT <= limit;
-      float mx = -INFINITY;
+      // row max of the raw scores (scale > 0), 8 independent partial maxima per 32 columns
+      float mxp[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) mxp[t] = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < KT / 32; ++c) {
         tmem_ld32(ts + 32 * c, r);
         tmem_ld_wait();
+        if (full_tile) {
 #pragma unroll
-        for (int t = 0; t < 32; ++t) {
-          const bool valid = full_tile || (key0 + 32 * c + t < limit);
-          if (valid) mx = fmaxf(mx, __uint_as_float(r[t]) * p.scale_log2);
+          for (int t = 0; t < 32; ++t) mxp[t & 7] = fmaxf(mxp[t & 7], __uint_as_float(r[t]));
+        } else {
+#pragma unroll
+          for (int t = 0; t < 32; ++t)
+            if (key0 + 32 * c + t < limit) mxp[t & 7] = fmaxf(mxp[t & 7], __uint_as_float(r[t]));
         }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]))) * p.scale_log2;
       const float m_new = fmaxf(m_run, mx);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m_run - m_use);  // 0 on the first tile
+      const float alpha = ex2(m_run - m_use);  // 0 on the first tile
       // the P buffer is free once the previous P.V has been issued and completed
       if (!mbar_wait(p_empty, (j & 1) ^ 1, p.status, 209)) { ok = false; break; }
-      float rowsum = 0.f;
+      float sump[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) sump[t] = 0.f;
 #pragma unroll 1
       for (int c = 0; c < KT / 32; ++c) {
         tmem_ld32(ts + 32 * c, r);
@@ -222,9 +239,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int t = 0; t < 32; t += 2) {
           const bool v0 = full_tile || (key0 + 32 * c + t < limit);
           const bool v1 = full_tile || (key0 + 32 * c + t + 1 < limit);
-          const float e0 = v0 ? exp2f(fmaf(__uint_as_float(r[t]), p.scale_log2, -m_use)) : 0.f;
-          const float e1 = v1 ? exp2f(fmaf(__uint_as_float(r[t + 1]), p.scale_log2, -m_use)) : 0.f;
-          rowsum += e0 + e1;
+          const float e0 = v0 ? ex2(fmaf(__uint_as_float(r[t]), p.scale_log2, -m_use)) : 0.f;
+          const float e1 = v1 ? ex2(fmaf(__uint_as_float(r[t + 1]), p.scale_log2, -m_use)) : 0.f;
+          sump[(t >> 1) & 7] += e0 + e1;
           pk[t / 2] = pack_half2(e0, e1);
         }
         // keys 32c..32c+31 -> half (c/2) of P, 16-byte units 4(c%2)..4(c%2)+3, swizzled by row
@@ -242,6 +259,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         mbar_arrive(&s_empty[sb]);
         mbar_arrive(p_full);
       }
+      const float rowsum = ((sump[0] + sump[1]) + (sump[2] + sump[3])) + ((sump[4] + sump[5]) + (sump[6] + sump[7]));
       l_run = fmaf(l_run, alpha, rowsum);
       m_run = m_new;
       if (j >= 1 && !consume_pv(j - 1, alpha_pend)) { ok = false; break; }
