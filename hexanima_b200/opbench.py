@@ -69,7 +69,7 @@ def main(argv=None):
 
     A = torch.randn(M, D, device=dev, generator=g).half()
     Amid = torch.randn(M, F, device=dev, generator=g).half()
-    qkv = torch.empty(M, 3 * D, device=dev).half()
+    qkv = (0.5 * torch.randn(M, 3 * D, device=dev, generator=g)).half()  # attention reads it before any qkv op
     mid = torch.empty(M, F, device=dev).half()
     o = torch.empty(M, D, device=dev).half()
     x = torch.randn(M, D, device=dev, generator=g)
@@ -87,7 +87,7 @@ def main(argv=None):
     ops["o"] = (lambda: h.gemm(A, M, mo, rt.EPI_RESID, lda=D, x=x, ldx=D, gate=gate, tile=a.tile), 2.0 * M * D * D, "TFLOP/s")
     if a.model == "anima":
         ctx = torch.randn(B * C, CD, device=dev, generator=g).half()
-        ckvb = torch.empty(B * C, 2 * D, device=dev).half()
+        ckvb = (0.5 * torch.randn(B * C, 2 * D, device=dev, generator=g)).half()
         mckv = mat(2 * D, CD)
         ops["ckv"] = (lambda: h.gemm(ctx, B * C, mckv, rt.EPI_RMS, lda=CD, out=ckvb, ldo=2 * D, gain0=gain, seg1=D,
                                      seg2=D, tile=a.tile), 2.0 * B * C * 2 * D * CD, "TFLOP/s")
