@@ -63,11 +63,39 @@ struct AParams {
   int* status;
 };
 
+// packed fp32 pairs (sm_100 f32x2 arithmetic: two lanes per instruction, each rounded like the scalar op)
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// three-input maximum (sm_100); like fmaxf, a NaN operand is ignored
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // max over 32 raw scores at keys kbase..kbase+31 into 8 partial maxima (keys >= limit skipped)
-__device__ __forceinline__ void max32(float (&mxp)[8], const uint32_t (&r)[32], bool full, int kbase, int limit) {
-  if (full) {
+template <bool FULL>
+__device__ __forceinline__ void max32(float (&mxp)[8], const uint32_t (&r)[32], int kbase, int limit) {
+  if constexpr (FULL) {
 #pragma unroll
-    for (int t = 0; t < 32; ++t) mxp[t & 7] = fmaxf(mxp[t & 7], __uint_as_float(r[t]));
+    for (int t = 0; t < 32; t += 2)
+      mxp[(t >> 1) & 7] = fmax3(mxp[(t >> 1) & 7], __uint_as_float(r[t]), __uint_as_float(r[t + 1]));
   } else {
 #pragma unroll
     for (int t = 0; t < 32; ++t)
@@ -75,16 +103,20 @@ __device__ __forceinline__ void max32(float (&mxp)[8], const uint32_t (&r)[32], 
   }
 }
 
-// p = 2^(s*scale_log2 - m) for 32 scores, fp16-packed into pk, partial sums into sump
-__device__ __forceinline__ void exp32(uint32_t (&pk)[16], float (&sump)[8], const uint32_t (&r)[32], float scale_log2,
-                                      float m, bool full, int kbase, int limit) {
+// p = 2^(s*scale_log2 - m) for 32 scores, fp16-packed into pk, pairwise partial sums into sum2
+template <bool FULL>
+__device__ __forceinline__ void exp32(uint32_t (&pk)[16], uint64_t (&sum2)[4], const uint32_t (&r)[32],
+                                      uint64_t scale2, uint64_t negm2, int kbase, int limit) {
 #pragma unroll
   for (int t = 0; t < 32; t += 2) {
-    const bool v0 = full || (kbase + t < limit);
-    const bool v1 = full || (kbase + t + 1 < limit);
-    const float e0 = v0 ? ex2(fmaf(__uint_as_float(r[t]), scale_log2, -m)) : 0.f;
-    const float e1 = v1 ? ex2(fmaf(__uint_as_float(r[t + 1]), scale_log2, -m)) : 0.f;
-    sump[(t >> 1) & 7] += e0 + e1;
+    float x0, x1;
+    f2unpack(ffma2(f2pack(__uint_as_float(r[t]), __uint_as_float(r[t + 1])), scale2, negm2), x0, x1);
+    float e0 = ex2(x0), e1 = ex2(x1);
+    if constexpr (!FULL) {
+      if (kbase + t >= limit) e0 = 0.f;
+      if (kbase + t + 1 >= limit) e1 = 0.f;
+    }
+    sum2[(t >> 1) & 3] = fadd2(sum2[(t >> 1) & 3], f2pack(e0, e1));
     pk[t / 2] = pack_half2(e0, e1);
   }
 }
@@ -138,7 +170,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&o_full[i], 1);
       mbar_init(&o_empty[i], SM_WARPS);
     }
-    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 64);
+    for (int i = 0; i < 8; ++i) mbar_init(&xbar[i], 2);  // the two warps of a row group
     mbar_init(drain, 1);
     fence_barrier_init();
   }
@@ -236,9 +268,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     const int row = g * 32 + lane;
     const uint32_t tl = static_cast<uint32_t>(g * 32) << 16;
     const int limit = p.nvalid;  // keys >= limit are masked
-    float o[HD / 2];
+    uint64_t o2[HD / 4];  // this half's 64 output dims as fp32 pairs
 #pragma unroll
-    for (int i = 0; i < HD / 2; ++i) o[i] = 0.f;
+    for (int i = 0; i < HD / 4; ++i) o2[i] = 0;
     float m_run = -INFINITY, l_run = 0.f, alpha_pend = 0.f;
     uint32_t sa[32], r[32];
     bool ok = true;
@@ -253,21 +285,24 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&o_empty[ob]);
+      const uint64_t a2 = f2pack(alpha, alpha);
 #pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        o[t] = fmaf(o[t], alpha, __uint_as_float(sa[t]));
-        o[32 + t] = fmaf(o[32 + t], alpha, __uint_as_float(r[t]));
+      for (int t = 0; t < 16; ++t) {
+        o2[t] = ffma2(o2[t], a2, f2pack(__uint_as_float(sa[2 * t]), __uint_as_float(sa[2 * t + 1])));
+        o2[16 + t] = ffma2(o2[16 + t], a2, f2pack(__uint_as_float(r[2 * t]), __uint_as_float(r[2 * t + 1])));
       }
       return true;
     };
-    // exchange one float per row with the other half: write, arrive, wait, read (parity slot `par`)
+    // exchange one float per row with the other half: write, arrive (one per warp), wait, read
     auto exchange = [&](int par, int phase, float mine, float& theirs) -> bool {
       xch[(par * 2 + hf) * 128 + row] = mine;
-      mbar_arrive(&xbar[par * 4 + g]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xbar[par * 4 + g]);
       if (!mbar_wait(&xbar[par * 4 + g], phase & 1, p.status, 213)) return false;
       theirs = xch[(par * 2 + (hf ^ 1)) * 128 + row];
       return true;
     };
+    const uint64_t scale2 = f2pack(p.scale_log2, p.scale_log2);
     for (int j = 0; j < nkt && ok; ++j) {
       const int pb = j & 1;
       if (!mbar_wait(s_full, j & 1, p.status, 208)) { ok = false; break; }
@@ -283,10 +318,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       float mxp[8];
 #pragma unroll
       for (int t = 0; t < 8; ++t) mxp[t] = -INFINITY;
-      max32(mxp, sa, full_tile, kown, limit);
-      max32(mxp, r, full_tile, kown + 32, limit);
-      const float pm = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      if (full_tile) {
+        max32<true>(mxp, sa, kown, limit);
+        max32<true>(mxp, r, kown + 32, limit);
+      } else {
+        max32<false>(mxp, sa, kown, limit);
+        max32<false>(mxp, r, kown + 32, limit);
+      }
+      const float pm = fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7]));
       float om;
       if (!exchange(j & 1, j >> 1, pm, om)) { ok = false; break; }
       const float mx = fmaxf(pm, om) * p.scale_log2;
@@ -295,24 +334,32 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       const float alpha = ex2(m_run - m_use);  // 0 on the first tile
       // P buffer pb is free once P.V of tile j-2 has completed
       if (!mbar_wait(&p_empty[pb], ((j >> 1) & 1) ^ 1, p.status, 209)) { ok = false; break; }
-      float sump[8];
-#pragma unroll
-      for (int t = 0; t < 8; ++t) sump[t] = 0.f;
+      uint64_t sum2[4] = {0, 0, 0, 0};
+      const uint64_t negm2 = f2pack(-m_use, -m_use);
       // keys 64hf + t -> P column 32hf + t/2 of buffer pb
       const uint32_t tp = tmem + tl + TM_P + pb * 64 + 32 * hf;
       {
         uint32_t pk[16];
-        exp32(pk, sump, sa, p.scale_log2, m_use, full_tile, kown, limit);
-        tmem_st16(tp, pk);
-        exp32(pk, sump, r, p.scale_log2, m_use, full_tile, kown + 32, limit);
-        tmem_st16(tp + 16, pk);
+        if (full_tile) {
+          exp32<true>(pk, sum2, sa, scale2, negm2, kown, limit);
+          tmem_st16(tp, pk);
+          exp32<true>(pk, sum2, r, scale2, negm2, kown + 32, limit);
+          tmem_st16(tp + 16, pk);
+        } else {
+          exp32<false>(pk, sum2, sa, scale2, negm2, kown, limit);
+          tmem_st16(tp, pk);
+          exp32<false>(pk, sum2, r, scale2, negm2, kown + 32, limit);
+          tmem_st16(tp + 16, pk);
+        }
       }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[pb]);
-      const float rowsum = ((sump[0] + sump[1]) + (sump[2] + sump[3])) + ((sump[4] + sump[5]) + (sump[6] + sump[7]));
-      l_run = fmaf(l_run, alpha, rowsum);
+      const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
+      float slo, shi;
+      f2unpack(s01, slo, shi);
+      l_run = fmaf(l_run, alpha, slo + shi);
       m_run = m_new;
       if (j >= 1 && !consume_pv(j - 1, alpha_pend)) { ok = false; break; }
       alpha_pend = alpha;
@@ -328,9 +375,13 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       __half* dst = p.o + (static_cast<size_t>(b) * p.Tq + q) * p.ldo + h * HD + 64 * hf;
       uint4* d4 = reinterpret_cast<uint4*>(dst);
 #pragma unroll
-      for (int u = 0; u < HD / 16; ++u)
-        d4[u] = make_uint4(pack_half2(o[8 * u] * inv, o[8 * u + 1] * inv), pack_half2(o[8 * u + 2] * inv, o[8 * u + 3] * inv),
-                           pack_half2(o[8 * u + 4] * inv, o[8 * u + 5] * inv), pack_half2(o[8 * u + 6] * inv, o[8 * u + 7] * inv));
+      for (int u = 0; u < HD / 16; ++u) {
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) f2unpack(o2[4 * u + e], v[2 * e], v[2 * e + 1]);
+        d4[u] = make_uint4(pack_half2(v[0] * inv, v[1] * inv), pack_half2(v[2] * inv, v[3] * inv),
+                           pack_half2(v[4] * inv, v[5] * inv), pack_half2(v[6] * inv, v[7] * inv));
+      }
     }
   }
 
