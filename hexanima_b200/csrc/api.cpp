@@ -907,6 +907,58 @@ int hx_weights_free(hx_handle hh, int wfd) {
   return HX_OK;
 }
 
+int hx_lora_fold(hx_handle hh, int wfd, int slot, const float* B, const float* A, int rank, float scale) {
+  hx_ctx* h = H(hh);
+  if (!h || !B || !A || slot < 0 || slot >= HX_NMATS || rank < 1 || rank > 128) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto it = h->weights.find(wfd);
+  if (it == h->weights.end()) return HX_E_NOWEIGHTS;
+  const Weights& W = *it->second;
+  if (!W.has[slot]) return HX_E_ARG;
+  const DevMat& M = W.mats[slot];
+  if (M.fmt != HX_FMT_Q8) return HX_E_FORMAT;
+  const bool lora_rows = W.model == HX_MODEL_MOSS && W.lora &&
+                         (slot == HX_W_Q || slot == HX_W_K || slot == HX_W_V || slot == HX_W_O || slot == HX_W_M1 ||
+                          slot == HX_W_M2);
+  const int k_base = M.K - (lora_rows ? 128 : 0);
+  const int row_mode = (W.model == HX_MODEL_MOSS && slot == HX_W_M1) ? 1 : 0;
+  const int floor_mode = W.model == HX_MODEL_ANIMA ? 1 : 0;
+  DevGuard g(h->device);
+  const cudaError_t e = lora_fold_launch(M, k_base, B, A, rank, scale, row_mode, floor_mode, h->stream);
+  return e == cudaSuccess ? HX_OK : e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA;
+}
+
+int hx_pack_apply_overlay(void* pack, size_t pack_bytes, const void* ovl, size_t ovl_bytes) {
+  if (!pack || !ovl || ovl_bytes < 4) return HX_E_ARG;
+  const uint8_t* o = static_cast<const uint8_t*>(ovl);
+  uint32_t n;
+  std::memcpy(&n, o, 4);
+  // pass 1: every record inside both buffers
+  size_t pos = 4;
+  for (uint32_t i = 0; i < n; ++i) {
+    if (ovl_bytes - pos < 12) return HX_E_FORMAT;
+    uint64_t off;
+    uint32_t len;
+    std::memcpy(&off, o + pos, 8);
+    std::memcpy(&len, o + pos + 8, 4);
+    pos += 12;
+    if (ovl_bytes - pos < len || off > pack_bytes || pack_bytes - off < len) return HX_E_FORMAT;
+    pos += len;
+  }
+  if (pos != ovl_bytes) return HX_E_FORMAT;
+  // pass 2: apply in file order
+  pos = 4;
+  for (uint32_t i = 0; i < n; ++i) {
+    uint64_t off;
+    uint32_t len;
+    std::memcpy(&off, o + pos, 8);
+    std::memcpy(&len, o + pos + 8, 4);
+    std::memcpy(static_cast<uint8_t*>(pack) + off, o + pos + 12, len);
+    pos += 12 + len;
+  }
+  return HX_OK;
+}
+
 // ---------------------------------------------------------------- blob layout
 int hx_blob_layout(int model, int ntok, int nctx, int batch, int D, int F, int Cd, int32_t* meta, int nmeta,
                    size_t* total) {

@@ -104,6 +104,10 @@ cudaError_t pad_cols_launch(const __half* src, __half* dst, int rows, int cols, 
 // weight repacking from the reference pack records (repack.cu)
 cudaError_t repack_tiles_launch(const uint8_t* rec, int nb, int kb, bool q8, void* dst, __half* scale, int row0,
                                 int nrows_total, int mode, cudaStream_t s);
+// scale * B * A folded into the base columns [0, k_base) of a q8 matrix, requantised per group
+// (lora.cu). row_mode 1: MOSS up_gate device row order; floor_mode 0 MOSS, 1 Anima scale floor.
+cudaError_t lora_fold_launch(const DevMat& W, int k_base, const float* B, const float* A, int rank, float lscale,
+                             int row_mode, int floor_mode, cudaStream_t s);
 int sm_count();
 
 }  // namespace hx

@@ -116,6 +116,8 @@ _SIGS = {
     "hx_weights_load": [_vp, _i, _vp, _sz, ctypes.POINTER(_i)],
     "hx_weights_bind": [_vp, ctypes.POINTER(hx_weight_desc), ctypes.POINTER(_i)],
     "hx_weights_free": [_vp, _i],
+    "hx_lora_fold": [_vp, _i, _i, _vp, _vp, _i, _f],
+    "hx_pack_apply_overlay": [_vp, _sz, _vp, _sz],
     "hx_blob_layout": [_i, _i, _i, _i, _i, _i, _i, _ip, _i, ctypes.POINTER(_sz)],
     "hx_mega_block": [_vp, _ip, _i, _i, _i, _vp, _i, _ip, _i, _ip],
     "hx_sp_unique_id": [_vp],
@@ -190,6 +192,13 @@ def modulation_noalloc(modA, modB, emb, lora, mod_out, nsite, D, stream=None):
     for callers that cannot call cudaMalloc (see include/hxdit.h). Scratch is a fixed static device array."""
     _check(lib().hx_modulation_noalloc(_ptr(modA), _ptr(modB), _ptr(emb), _ptr(lora), _ptr(mod_out), nsite, D, stream),
            "hx_modulation_noalloc")
+
+
+def pack_apply_overlay(pack, ovl):
+    """Apply a blkNN.ovl LoRA overlay (bytes) to a block pack held in a writable buffer (bytearray), in place."""
+    pb = (ctypes.c_char * len(pack)).from_buffer(pack)
+    ob = ctypes.create_string_buffer(bytes(ovl), len(ovl))
+    _check(lib().hx_pack_apply_overlay(ctypes.addressof(pb), len(pack), ob, len(ovl)), "hx_pack_apply_overlay")
 
 
 def sp_unique_id():
@@ -289,6 +298,10 @@ class Handle:
 
     def weights_free(self, wfd):
         _check(lib().hx_weights_free(self.h, wfd), "hx_weights_free")
+
+    def lora_fold(self, wfd, slot, B_dev, A_dev, rank, scale=1.0):
+        """Fold scale * B[N][rank] @ A[rank][K_base] (device fp32) into the q8 matrix `slot` of wfd, in place."""
+        _check(lib().hx_lora_fold(self.h, wfd, slot, _ptr(B_dev), _ptr(A_dev), rank, scale), "hx_lora_fold")
 
     # -------------------------------------------------------------- block / chain
     def mega_block(self, meta, wfd, bfd, mod=None, ntimes=0):

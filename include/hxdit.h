@@ -126,6 +126,21 @@ HX_API int hx_weights_load(hx_handle h, int model, const void* pack, size_t byte
 /* Bind caller-owned device arrays already in the device layout (no copy; they must outlive use). */
 HX_API int hx_weights_bind(hx_handle h, const hx_weight_desc* desc, int* wfd);
 HX_API int hx_weights_free(hx_handle h, int wfd);
+/* Fold scale * B * A (a LoRA delta of rank 1..128) into the q8 matrix `slot` of weight set wfd, in
+ * place: dequantise, add, and requantise every K-group with the pack rule of the reference's fold
+ * tool (moss/mossrun/lorafold.cpp:138-156 `quant`; scale floor 6.2e-5 for MOSS, 0 -> 1.0 for Anima).
+ * Only the base columns change: with MOSS LoRA K rows (desc.lora) the first K-128.
+ *   B: device fp32 [N][rank] in the matrix's logical row order (MOSS up_gate: rows [0,F) up,
+ *      [F,2F) gate; Anima fused qkv: q, k, v rows).   A: device fp32 [rank][K_base].
+ * The base-tile variant of the reference's rank-128-slot fold (lorafold.cpp:200-284). Bound
+ * (caller-owned) weights are modified too. Runs on the handle's stream. */
+HX_API int hx_lora_fold(hx_handle h, int wfd, int slot, const float* B_dev, const float* A_dev, int rank, float scale);
+
+/* Apply a LoRA overlay file (blkNN.ovl written by moss/make_lora_overlay.py:54-56 and
+ * moss/mossrun/lorafold.cpp:284-288: u32 n, then n records of u64 pack offset, u32 length, bytes)
+ * to a block pack in host memory before hx_weights_load. All records are checked first; on a
+ * truncated overlay or a record outside the pack it returns HX_E_FORMAT and leaves the pack as it was. */
+HX_API int hx_pack_apply_overlay(void* pack, size_t pack_bytes, const void* ovl, size_t ovl_bytes);
 
 /* ------------------------------------------------------------------ the per-block operator */
 /* Anima meta[] slots: byte offsets into the blob buffer, then scalars.

@@ -211,3 +211,35 @@ def interleave32(up_kn, gate_kn):
     """Pack column order of MOSS up_gate (export_moss.py:17-19): 32-column blocks (up_j, gate_j)."""
     K, F = up_kn.shape
     return np.stack((up_kn.reshape(K, F // 32, 32), gate_kn.reshape(K, F // 32, 32)), 2).reshape(K, 2 * F)
+
+
+# ---------------------------------------------------------------- LoRA fold into q8 base tiles
+def lora_fold_q8(u, scale, group, B, A, lscale=1.0, floor=F16_FLOOR_MOSS, k_base=None):
+    """Device q8 (u8 [N][K], fp16 scale [K/group][N]) with lscale * B[N][r] @ A[r][k_base] added to
+    columns [0, k_base), each group requantised with the quant_q8 rule (the rule of the reference's fold
+    tool, moss/mossrun/lorafold.cpp:138-156). B rows are in device row order.
+
+    The arithmetic order is part of the definition (the device kernel follows it): the rank sum runs
+    r = 0, 1, ... with each product and each sum rounded to float32, then v = q*s + fl(lscale * sum)."""
+    N, K = u.shape
+    kb = K if k_base is None else k_base
+    B = np.asarray(B, np.float32)
+    A = np.asarray(A, np.float32)
+    acc = np.zeros((N, kb), np.float32)
+    for r in range(B.shape[1]):
+        acc = acc + np.outer(B[:, r], A[r])
+    sc = np.repeat(scale[:kb // group].T.astype(np.float32), group, axis=1)
+    v = (u[:, :kb].astype(np.float32) - np.float32(128)) * sc + np.float32(lscale) * acc
+    nu, ns = quant_q8(v, group, floor)
+    out_u, out_s = u.copy(), scale.copy()
+    out_u[:, :kb] = nu
+    out_s[:kb // group] = ns
+    return out_u, out_s
+
+
+def situ_logical_rows(n_rows):
+    """Device row r of a MOSS up_gate matrix -> its logical row ([0,F) up, [F,2F) gate); inverse view of situ_rows."""
+    F = n_rows // 2
+    r = np.arange(n_rows)
+    o = (r // 256) * 128 + (r % 256) % 128
+    return np.where(r % 256 < 128, o, F + o)
