@@ -37,6 +37,7 @@ constexpr size_t kMossPack = 135397376u;      // W_TOTAL, moss/hexagon/mega/blk_
 
 struct Weights {
   int model = 0, D = 0, F = 0, Cd = 0, H = 0, lora = 0;
+  int proj = 0;  // MOSS text projection weights (MODE 2 only): W_O = [D][Cd + 128], Cd = text width
   DevMat mats[HX_NMATS];
   bool has[HX_NMATS] = {};
   const float* gain = nullptr;
@@ -280,6 +281,30 @@ int load_moss(hx_ctx* h, const uint8_t* pack, size_t bytes, Weights& W) {
   return HX_OK;
 }
 
+// MOSS text projection pack (export_moss.py:61-65 `pack_proj`): [96 nb][132 kb] q8 tiles of
+// [Wp^T ; bias row, 127 zero rows] at offset 0, padded with zeros to the block-pack size.
+int load_moss_proj(hx_ctx* h, const uint8_t* pack, size_t bytes, Weights& W) {
+  const int D = 3072, TW = 4096;
+  const size_t need = static_cast<size_t>(D / 32) * ((TW + 128) / 32) * 1152;
+  if (bytes != kMossPack && bytes != need) return HX_E_FORMAT;
+  W.model = HX_MODEL_MOSS;
+  W.proj = 1;
+  W.D = D;
+  W.F = 8192;
+  W.Cd = TW;
+  W.H = 24;
+  W.lora = 1;
+  int rc;
+  if ((rc = alloc_mat(W, HX_W_O, HX_FMT_Q8, D, TW + 128, 32))) return rc;
+  uint8_t* dpack = nullptr;
+  CK(cudaMalloc(&dpack, need));
+  CK(cudaMemcpyAsync(dpack, pack, need, cudaMemcpyHostToDevice, h->stream));
+  rc = repack_into(W, HX_W_O, dpack, 0, D / 32, (TW + 128) / 32, true, 0, 0, h->stream);
+  cudaStreamSynchronize(h->stream);
+  cudaFree(dpack);
+  return rc;
+}
+
 // ---------------------------------------------------------------- block orchestration
 struct Stage {
   hx_ctx* h;
@@ -425,7 +450,7 @@ int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, 
   const int T = meta[HX_S_NTOK];
   const int nvalid = meta[HX_S_NVALID] > 0 ? meta[HX_S_NVALID] : T * (meta[HX_S_SP] > 1 ? meta[HX_S_SP] : 1);
   const int B = meta[HX_S_BATCH] > 0 ? meta[HX_S_BATCH] : 1;
-  if (meta[HX_S_MODE] != 0) return HX_E_ARG;  // text-refiner / projection modes are not built
+  const int mode = meta[HX_S_MODE];  // 0 DiT block, 1 text refiner (no LoRA-A GEMMs), 2 text projection
   const int rows = B * T;
   cudaStream_t s = h->stream;
   float* x = reinterpret_cast<float*>(blob + meta[HX_S_X]);
@@ -446,10 +471,24 @@ int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, 
     lu = hptr(blob, meta[HX_S_LU]);
     ld = hptr(blob, meta[HX_S_LD]);
   }
+  if (mode == 2) {  // x += gate_a * (text . Wp + bias)   (moss/hexagon/mega/blk.c:229-233)
+    GemmArgs g = gargs(h, hbuf, W.Cd, rows, &W.mats[HX_W_O], EPI_RESID);
+    g.K1 = W.Cd;
+    g.A2 = lq;
+    g.lda2 = 384;
+    g.x = x;
+    g.ldx = D;
+    g.gate = gt_a;
+    g.vec_bstride = 0;
+    CKL(gemm_launch(g, s));
+    st.tick();
+    return HX_OK;
+  }
+  const bool run_a = lora && mode == 0;  // MODE 1: the L buffers hold the host's bias selector
   // ---- attention half
   CKL(rmsmod_launch(x, hbuf, rows, D, gain + 256, sh_a, sc_a, 0, T, 1e-6f, s));
   if (st.tick()) return HX_OK;
-  if (lora) {
+  if (run_a) {
     GemmArgs ga = gargs(h, hbuf, D, rows, &W.mats[HX_W_AQKV], EPI_STORE);
     ga.out = lq;
     ga.ldo = 384;
@@ -503,7 +542,7 @@ int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, 
   }
   if (st.tick()) return HX_OK;
   {
-    if (lora) {
+    if (run_a) {
       GemmArgs ga = gargs(h, obuf, D, rows, &W.mats[HX_W_AO], EPI_STORE);
       ga.out = lo;
       ga.ldo = 128;
@@ -525,7 +564,7 @@ int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, 
   CKL(rmsmod_launch(x, hbuf, rows, D, gain + 256 + D, sh_f, sc_f, 0, T, 1e-6f, s));
   if (st.tick()) return HX_OK;
   {
-    if (lora) {
+    if (run_a) {
       GemmArgs ga = gargs(h, hbuf, D, rows, &W.mats[HX_W_AUG], EPI_STORE);
       ga.out = lu;
       ga.ldo = 128;
@@ -543,7 +582,7 @@ int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, 
   }
   if (st.tick()) return HX_OK;
   {
-    if (lora) {
+    if (run_a) {
       GemmArgs ga = gargs(h, mid, F, rows, &W.mats[HX_W_ADN], EPI_STORE);
       ga.out = ld;
       ga.ldo = 128;
@@ -590,6 +629,15 @@ int check_meta(const Weights& W, const int32_t* meta, int nmeta, size_t blob_byt
     if (sp > 1 && B != 1) return HX_E_ARG;
     if (meta[HX_S_NVALID] < 0 || static_cast<size_t>(meta[HX_S_NVALID]) > T * (sp > 1 ? sp : 1)) return HX_E_ARG;
     const size_t D = W.D, F = W.F, R = B * T;
+    const int mode = meta[HX_S_MODE];
+    if (mode < 0 || mode > 2 || (mode == 2) != (W.proj != 0) || (mode == 1 && !W.lora)) return HX_E_ARG;
+    if (W.proj) {  // MODE 2 reads H [R][Cd] and the LQ bias selector, adds into X
+      if (!in(meta[HX_S_X], R * D * 4) || !in(meta[HX_S_H], R * W.Cd * 2) || !in(meta[HX_S_LQ], R * 384 * 2))
+        return HX_E_RANGE;
+      for (int slot : {HX_S_X, HX_S_H, HX_S_LQ})
+        if (meta[slot] % 256) return HX_E_RANGE;
+      return HX_OK;
+    }
     if (!in(meta[HX_S_X], R * D * 4) || !in(meta[HX_S_COS], T * 256) || !in(meta[HX_S_SIN], T * 256) ||
         !in(meta[HX_S_H], R * D * 2) || !in(meta[HX_S_Q], R * 3 * D * 2) || !in(meta[HX_S_O], R * D * 2) ||
         !in(meta[HX_S_MID], R * F * 2))
@@ -847,7 +895,8 @@ int hx_weights_load(hx_handle hh, int model, const void* pack, size_t bytes, int
   auto W = std::make_unique<Weights>();
   int rc = model == HX_MODEL_ANIMA ? load_anima(h, static_cast<const uint8_t*>(pack), bytes, *W)
            : model == HX_MODEL_MOSS ? load_moss(h, static_cast<const uint8_t*>(pack), bytes, *W)
-                                    : HX_E_ARG;
+           : model == HX_MODEL_MOSS_PROJ ? load_moss_proj(h, static_cast<const uint8_t*>(pack), bytes, *W)
+                                         : HX_E_ARG;
   if (rc) {
     for (void* p : W->owned) cudaFree(p);
     return rc;
@@ -870,8 +919,21 @@ int hx_weights_bind(hx_handle hh, const hx_weight_desc* d, int* wfd) {
   W->gain = d->gain;
   W->modA = static_cast<const __half*>(d->modA);
   W->modB = static_cast<const __half*>(d->modB);
-  if (W->D <= 0 || W->D % 128 || W->F <= 0 || W->F % 256 || W->H * 128 != W->D || !W->gain) return HX_E_ARG;
   std::vector<int> need;
+  if (d->model == HX_MODEL_MOSS_PROJ) {  // text projection: W_O [D][Cd + 128] only
+    W->model = HX_MODEL_MOSS;
+    W->proj = 1;
+    W->lora = 1;
+    if (W->D <= 0 || W->D % 128 || W->Cd <= 0 || W->Cd % 64 || W->H * 128 != W->D) return HX_E_ARG;
+    if (!valid_mat(d->mats[HX_W_O]) || d->mats[HX_W_O].n != W->D || d->mats[HX_W_O].k != W->Cd + 128) return HX_E_ARG;
+    W->mats[HX_W_O] = to_devmat(d->mats[HX_W_O]);
+    W->has[HX_W_O] = true;
+    std::lock_guard<std::mutex> lk(h->mu);
+    *wfd = h->next_fd++;
+    h->weights[*wfd] = std::move(W);
+    return HX_OK;
+  }
+  if (W->D <= 0 || W->D % 128 || W->F <= 0 || W->F % 256 || W->H * 128 != W->D || !W->gain) return HX_E_ARG;
   if (d->model == HX_MODEL_ANIMA) {
     need = {HX_W_QKV, HX_W_O, HX_W_CQ, HX_W_CKV, HX_W_CO, HX_W_M1, HX_W_M2};
     if (W->Cd <= 0 || W->Cd % 64) return HX_E_ARG;
@@ -999,7 +1061,7 @@ int hx_blob_layout(int model, int ntok, int nctx, int batch, int D, int F, int C
     place(HX_S_COS, static_cast<size_t>(ntok) * 64 * 4);
     place(HX_S_SIN, static_cast<size_t>(ntok) * 64 * 4);
     place(HX_S_CS, 6ull * D * 4);  // mod vectors when the call passes none
-    place(HX_S_H, R * D * 2);
+    place(HX_S_H, R * static_cast<size_t>(Cd > D ? Cd : D) * 2);  // MODE 2 reads text rows of width Cd
     place(HX_S_Q, R * 3 * D * 2);
     meta[HX_S_K] = meta[HX_S_Q];
     meta[HX_S_V] = meta[HX_S_Q];

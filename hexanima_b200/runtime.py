@@ -23,7 +23,7 @@ HX_E_SCRATCH = -9
 ERRORS = {-1: "HX_E_ARG", -2: "HX_E_CUDA", -5: "HX_E_NOWEIGHTS", -6: "HX_E_NOBLOB", -7: "HX_E_RANGE",
           -8: "HX_E_FORMAT", -9: "HX_E_SCRATCH", -77: "HX_E_TIMEOUT"}
 
-MODEL_ANIMA, MODEL_MOSS = 1, 2
+MODEL_ANIMA, MODEL_MOSS, MODEL_MOSS_PROJ = 1, 2, 3
 FMT_F16, FMT_Q8, FMT_Q4A, FMT_Q4 = 0, 1, 2, 3
 EPI_STORE, EPI_RESID, EPI_GELU, EPI_RMS, EPI_SITU, EPI_STORE32 = 0, 1, 2, 3, 5, 6
 (W_QKV, W_O, W_CQ, W_CKV, W_CO, W_M1, W_M2, W_Q, W_K, W_V, W_AQKV, W_AO, W_AUG, W_ADN) = range(14)

@@ -46,6 +46,9 @@ extern "C" {
 /* ------------------------------------------------------------------ models and weight formats */
 #define HX_MODEL_ANIMA 1    /* hexagon/mega: D 2048, 16 heads, self + cross attention, GELU MLP */
 #define HX_MODEL_MOSS 2     /* moss/hexagon/mega: D 3072, 24 heads, joint attention, SiTU MLP, LoRA K tiles */
+#define HX_MODEL_MOSS_PROJ 3 /* MOSS text projection (mode 2): text_embedder.proj 4096 -> 3072 + bias, the pack of
+                               moss/export_moss.py:61-65 ([96 nb][132 kb] q8 tiles at offset 0, padded to the
+                               block-pack size, or unpadded); the weight set serves only meta MODE 2 */
 
 #define HX_FMT_F16 0        /* fp16 W[N][K] */
 #define HX_FMT_Q8 1         /* u8 W[N][K] offset binary (q+128), fp16 scale[K/group][N], group 32|64 */
@@ -164,7 +167,14 @@ enum {
 /* MOSS meta[] slots (moss/hexagon/mega/blk_meta.h:3-4). Blob layout:
  *   X fp32 [B][NTOK][D]; COS, SIN fp32 [NTOK][64]; H fp16 [B*NTOK][D]; Q fp16 [B*NTOK][3D] (fused);
  *   O fp16 [B*NTOK][D]; MID fp16 [B*NTOK][F]; LQ fp16 [B*NTOK][384]; LO, LU, LD fp16 [B*NTOK][128];
- *   mod: fp32 [6][D] (shift_a, scale_a, gate_a, shift_f, scale_f, gate_f) passed by the call or at CS. */
+ *   mod: fp32 [6][D] (shift_a, scale_a, gate_a, shift_f, scale_f, gate_f) passed by the call or at CS.
+ * MODE (moss/hexagon/mega/blk_meta.h:4, blk.c:229-237):
+ *   0  DiT block.
+ *   1  text-refiner block: the LoRA-A GEMMs are skipped; the host fills LQ/LO/LU/LD with the bias
+ *      selector (fp16 1.0 in column 0 of every 128-column part, 0 elsewhere) so the pack's LoRA K rows
+ *      (row 0 = bias, export_moss.py:43-59) add the biases; mod = (0, 0, 1, 0, 0, 1) rows.
+ *   2  text projection with a HX_MODEL_MOSS_PROJ weight set: X += gate_a * (H . Wp + bias), H fp16
+ *      [B*NTOK][text width] (the Cd of hx_blob_layout, 4096), the bias through the LQ selector. */
 enum {
   HX_S_X = 0, HX_S_COS, HX_S_SIN, HX_S_H, HX_S_Q, HX_S_K, HX_S_V, HX_S_O, HX_S_T, HX_S_MID,
   HX_S_LQ, HX_S_LO, HX_S_LU, HX_S_LD, HX_S_NTOK, HX_S_NVALID, HX_S_STOP, HX_S_NW, HX_S_REL,
@@ -178,8 +188,8 @@ enum {
 };
 
 /* Fill meta[] with a blob layout (megarun.cpp:42-57 layout()) for `batch` images; *total = bytes.
- * nmeta must be >= HX_A_NMETA_EXT (Anima) or HX_S_NMETA_EXT (MOSS). For MOSS, nctx is unused and
- * the mod vectors go to the CS slot. */
+ * nmeta must be >= HX_A_NMETA_EXT (Anima) or HX_S_NMETA_EXT (MOSS). For MOSS, nctx is unused, the mod
+ * vectors go to the CS slot, and a Cd above D (the text width of MODE 2) widens the H region to Cd. */
 HX_API int hx_blob_layout(int model, int ntok, int nctx, int batch, int D, int F, int Cd, int32_t* meta, int nmeta,
                    size_t* total);
 

@@ -8,7 +8,10 @@ Restates moss/moss_ref.py (pinned against it by tests/golden/moss_block.npz):
   attn         moss_ref.py:41-46   per-head rms(q|k) * gain, rotate, softmax(q k^T / sqrt(128)) v
   lin          moss_ref.py:48-54   x W^T (+ b) (+ s (x A^T) B^T)
   block        moss_ref.py:56-67   mod rows: shift_a, scale_a, gate_a, shift_f, scale_f, gate_f
-and the q8-pack-aware staged form of mkblk_test.py:38-55 (LoRA as extra K tiles: [x | x A] @ [W ; s B^T],
+  text_block   moss_ref.py:81-89   refiner block: rms, qkv + bias, attn, proj + bias, rms, SiTU(up, gate) + biases
+  text_refine  moss_ref.py:91-94   text_embedder.proj (4096 -> D) + bias, then two text blocks
+  time_vecs    moss_ref.py:96-105  cos|sin(t * 10000^(-i/128)), silu MLP, shared block / head modulation
+(pinned by tests/golden/moss_text.npz) and the q8-pack-aware staged form of mkblk_test.py:38-55 (LoRA as extra K tiles: [x | x A] @ [W ; s B^T],
 attention scale 1.0 with the q gain pre-divided by sqrt(128)).
 """
 import math
@@ -87,18 +90,35 @@ def block(x, mod, sin, cos, g, i, lora=None, heads=24):
     return x + lin(situ(h, gt), g(p + "proj.ffn_down.weight"), lora=L("ffn_down")) * gf
 
 
-def block_dev(x, mod, cos64, sin64, mats, gain, nvalid=None, lora=True, heads=None):
+def selector(shape_lead, width):
+    """The MODE 1 bias selector of an L buffer: 1.0 in column 0 of every 128-column part (mossrun.cpp:205-209)."""
+    t = torch.zeros(*shape_lead, width)
+    t[..., 0::128] = 1.0
+    return t
+
+
+def block_dev(x, mod, cos64, sin64, mats, gain, nvalid=None, lora=True, heads=None, refiner=False):
     """Staged, device-weight form (mkblk_test.py:38-55): every matrix is the [N][K'] operand the GPU
     multiplies (LoRA-B rows appended along K when lora), A matrices [r][K]; gain = [q/sqrt(128), k,
-    norm1, norm2]; up_gate rows grouped per 256 (128 up, 128 gate). x [B, T, D]; cos64/sin64 [T][64]."""
+    norm1, norm2]; up_gate rows grouped per 256 (128 up, 128 gate). x [B, T, D]; cos64/sin64 [T][64].
+    refiner: MODE 1 (moss/hexagon/mega/blk.c:237) - the L operands are the bias selector, not y A^T."""
     B, T, D = x.shape
     H = heads or D // HD
     sa, ca, ga, sf, cf, gf = mod
     qg, kg, n1, n2 = gain[:128], gain[128:256], gain[256:256 + D], gain[256 + D:256 + 2 * D]
     cat = lambda a, b: torch.cat((a, b), -1)
+    if refiner:
+        sel = {k: (lambda y, n=n: selector(y.shape[:-1], n)) for k, n in (("aqkv", 384), ("ao", 128), ("aug", 128),
+                                                                          ("adn", 128))}
+        mats = dict(mats)
+        for k in sel:
+            mats[k] = None
+    else:
+        sel = {}
+    LA = lambda y, name: sel[name](y) if name in sel else y @ mats[name].T
     y = rms(x, n1) * (1 + ca) + sa
     if lora:
-        Lq = y @ mats["aqkv"].T
+        Lq = LA(y, "aqkv")
         q = cat(y, Lq[..., 0:128]) @ mats["q"].T
         k = cat(y, Lq[..., 128:256]) @ mats["k"].T
         v = cat(y, Lq[..., 256:384]) @ mats["v"].T
@@ -115,14 +135,14 @@ def block_dev(x, mod, cos64, sin64, mats, gain, nvalid=None, lora=True, heads=No
     if nvalid is not None and nvalid < T:
         sc[..., nvalid:] = float("-inf")
     a = torch.einsum("bhqk,bkhd->bqhd", torch.softmax(sc, -1), v).reshape(B, T, D)
-    o = (cat(a, a @ mats["ao"].T) if lora else a) @ mats["o"].T
+    o = (cat(a, LA(a, "ao")) if lora else a) @ mats["o"].T
     x = x + o * ga
     y2 = rms(x, n2) * (1 + cf) + sf
-    ug = (cat(y2, y2 @ mats["aug"].T) if lora else y2) @ mats["ug"].T  # [B, T, 2F], grouped per 256
+    ug = (cat(y2, LA(y2, "aug")) if lora else y2) @ mats["ug"].T  # [B, T, 2F], grouped per 256
     F = ug.shape[-1] // 2
     g4 = ug.view(B, T, F // 128, 2, 128)
     mid = situ(g4[:, :, :, 0], g4[:, :, :, 1]).reshape(B, T, F)
-    dn = (cat(mid, mid @ mats["adn"].T) if lora else mid) @ mats["dn"].T
+    dn = (cat(mid, LA(mid, "adn")) if lora else mid) @ mats["dn"].T
     return x + dn * gf
 
 
@@ -196,3 +216,107 @@ def pack_mats(pack, D=3072, F=8192):
     mats["ug"] = torch.cat((up.view(F // 128, 128, -1), gate.view(F // 128, 128, -1)), 1).reshape(2 * F, -1)
     gain = torch.from_numpy(np.frombuffer(pack[off:off + (256 + 2 * D) * 4], np.float32).copy())
     return mats, gain
+
+
+# ---------------------------------------------------------------- text side and sampler glue
+def text_block(x, p, sin, cos, g, heads=24):
+    """moss_ref.text_block: x [N, D]; weights g(p + name) with biases."""
+    h = rms(x, g(p + "norm1.weight"))
+    q, k, v = lin(h, g(p + "qkv.weight"), g(p + "qkv.bias")).chunk(3, -1)
+    a = attn(q, k, v, sin, cos, g(p + "q_norm.weight"), g(p + "k_norm.weight"), heads)
+    x = x + lin(a, g(p + "proj.weight"), g(p + "proj.bias"))
+    y = rms(x, g(p + "norm2.weight"))
+    up = lin(y, g(p + "ffn_up.weight"), g(p + "ffn_up.bias"))
+    gate = lin(y, g(p + "ffn_gate.weight"), g(p + "ffn_gate.bias"))
+    return x + lin(situ(up, gate), g(p + "ffn_down.weight"), g(p + "ffn_down.bias"))
+
+
+def text_refine(txt, sin_t, cos_t, g, heads=24):
+    """moss_ref.text_refine: txt [T, 4096] -> [T, D]."""
+    x = lin(txt, g("text_embedder.proj.weight"), g("text_embedder.proj.bias"))
+    for i in range(2):
+        x = text_block(x, f"text_embedder.blocks.{i}.", sin_t, cos_t, g, heads)
+    return x
+
+
+def time_vecs(t, g):
+    """moss_ref.time_vecs: -> mod [6, D], head [2, D] (code t; embedding in float64 then float32)."""
+    half = 128
+    freq = 10000 ** (-torch.arange(half, dtype=torch.float64) / half)
+    ph = float(t) * freq
+    e = torch.cat((ph.cos(), ph.sin())).float()
+    a = torch.nn.functional.silu(e @ g("time_embedding.0.weight").T + g("time_embedding.0.bias"))
+    tm = a @ g("time_embedding.2.weight").T + g("time_embedding.2.bias")
+    mod = tm @ g("shared_block_modulation.weight").T + g("shared_block_modulation.bias")
+    head = tm @ g("video_head_modulation.weight").T + g("video_head_modulation.bias")
+    return mod.view(6, -1), head.view(2, -1)
+
+
+def init_text_weights(seed, D=3072, F=256, TW=4096, std=0.02, blocks=2):
+    """Seeded synthetic text_embedder (moss_ref naming): proj TW -> D and `blocks` refiner blocks."""
+    gen = torch.Generator().manual_seed(seed)
+    n = lambda *s: torch.randn(*s, generator=gen) * std
+    w = {"text_embedder.proj.weight": n(D, TW), "text_embedder.proj.bias": n(D)}
+    for i in range(blocks):
+        p = f"text_embedder.blocks.{i}."
+        w.update({p + "norm1.weight": 1 + n(D), p + "norm2.weight": 1 + n(D), p + "q_norm.weight": 1 + n(HD),
+                  p + "k_norm.weight": 1 + n(HD), p + "qkv.weight": n(3 * D, D), p + "qkv.bias": n(3 * D),
+                  p + "proj.weight": n(D, D), p + "proj.bias": n(D), p + "ffn_up.weight": n(F, D),
+                  p + "ffn_up.bias": n(F), p + "ffn_gate.weight": n(F, D), p + "ffn_gate.bias": n(F),
+                  p + "ffn_down.weight": n(D, F), p + "ffn_down.bias": n(D)})
+    return w
+
+
+def init_time_weights(seed, D=3072, std=0.02):
+    """Seeded synthetic time_embedding / modulation weights (moss_ref naming)."""
+    gen = torch.Generator().manual_seed(seed)
+    n = lambda *s: torch.randn(*s, generator=gen) * std
+    return {"time_embedding.0.weight": n(D, 256), "time_embedding.0.bias": n(D),
+            "time_embedding.2.weight": n(D, D), "time_embedding.2.bias": n(D),
+            "shared_block_modulation.weight": n(6 * D, D), "shared_block_modulation.bias": n(6 * D),
+            "video_head_modulation.weight": n(2 * D, D), "video_head_modulation.bias": n(2 * D)}
+
+
+def build_refiner_pack(w, i):
+    """Refiner block pack (export_moss.py:43-59 `pack_refiner`): the block layout of build_pack with the
+    biases in row 0 of the 128 LoRA K rows (scale 1) and zero LoRA-A matrices."""
+    p = f"text_embedder.blocks.{i}."
+    D = w[p + "norm1.weight"].shape[0]
+    qkv, qkvb = w[p + "qkv.weight"], w[p + "qkv.bias"]
+
+    def bias_lora(b, fan_in):
+        B = torch.zeros(b.shape[0], 128)
+        B[:, 0] = b
+        return (torch.zeros(128, fan_in), B, 1.0)
+
+    F = w[p + "ffn_up.weight"].shape[0]
+    blk = {"layers.0.proj.q.weight": qkv[:D], "layers.0.proj.k.weight": qkv[D:2 * D],
+           "layers.0.proj.v.weight": qkv[2 * D:], "layers.0.proj.o.weight": w[p + "proj.weight"],
+           "layers.0.proj.ffn_up_gate.weight": torch.cat((w[p + "ffn_up.weight"], w[p + "ffn_gate.weight"]), 0),
+           "layers.0.proj.ffn_down.weight": w[p + "ffn_down.weight"],
+           "layers.0.q_norm.weight": w[p + "q_norm.weight"], "layers.0.k_norm.weight": w[p + "k_norm.weight"],
+           "layers.0.norm1.weight": w[p + "norm1.weight"], "layers.0.norm2.weight": w[p + "norm2.weight"]}
+    lora = {"q": bias_lora(qkvb[:D], D), "k": bias_lora(qkvb[D:2 * D], D), "v": bias_lora(qkvb[2 * D:], D),
+            "o": bias_lora(w[p + "proj.bias"], D),
+            "ffn_up_gate": bias_lora(torch.cat((w[p + "ffn_up.bias"], w[p + "ffn_gate.bias"])), D),
+            "ffn_down": bias_lora(w[p + "ffn_down.bias"], F)}
+    return build_pack(blk, lora)
+
+
+def build_proj_pack(w, pad_to=135397376):
+    """Text projection pack (export_moss.py:61-65 `pack_proj`): q8 tiles of [Wp^T ; bias, 127 zero rows]
+    ([D/32 nb][(TW+128)/32 kb]) padded with zeros to the block-pack size."""
+    from .packs import F16_FLOOR_MOSS, q8tiles, wt16
+    Wp, b = w["text_embedder.proj.weight"], w["text_embedder.proj.bias"]
+    B = torch.zeros(128, Wp.shape[0])
+    B[0] = b
+    d = q8tiles(wt16(torch.cat((Wp.T, B), 0).numpy()), F16_FLOOR_MOSS)
+    return d + bytes(max(0, pad_to - len(d)))
+
+
+def proj_mat(pack, D=3072, TW=4096):
+    """Device-operand view of a projection pack: [D][TW + 128] fp32 of fp16(q*s)."""
+    from .packs import dequant_q8_f16
+    size = (D // 32) * ((TW + 128) // 32) * 1152
+    w = dequant_q8_f16(pack[:size], D // 32, (TW + 128) // 32).astype(np.float32)   # [K][N]
+    return torch.from_numpy(np.ascontiguousarray(w.T))

@@ -13,7 +13,8 @@ What is run from the reference (its code, not a restatement):
   moss/mkblk_test.py            unpack (q8 record decode); module-level code loads model files, so
                                 the function is compiled out of its source with ast
   moss/export_te.py             q4a_tiles, unpack_q4a
-  moss/moss_ref.py              block, rope_tables on seeded synthetic weights (lora off and on)
+  moss/moss_ref.py              block, rope_tables on seeded synthetic weights (lora off and on);
+                                text_block, text_refine and time_vecs (moss_text.npz)
 """
 import ast
 import os
@@ -88,6 +89,23 @@ def main():
         out[f"{tag}_w_sum"] = float(sum(v.double().sum() for v in w.values()))
         out[f"{tag}_out"] = y.numpy()
     np.savez_compressed(os.path.join(HERE, "moss_block.npz"), **out)
+
+    # ------------------------------------------------------------ MOSS text side (moss_ref.text_block / text_refine /
+    # time_vecs): refiner at D 3072 (24 heads are fixed in moss_ref.attn), FFN 256; time_vecs at D 256
+    Tt = 20
+    s_t, c_t = moss_ref.rope_tables(0, 1, Tt, bands)           # text rows only: coords (0, i, 0, 0)
+    wt = om.init_text_weights(21, D=3072, F=256)
+    gen = torch.Generator().manual_seed(121)
+    xt = torch.randn(Tt, 3072, generator=gen)
+    txt = torch.randn(Tt, 4096, generator=gen)
+    g = lambda n: wt[n]
+    tb = moss_ref.text_block(xt, "text_embedder.blocks.0.", s_t, c_t, g)
+    tr = moss_ref.text_refine(txt, s_t, c_t, g)
+    wtime = om.init_time_weights(22, D=256)
+    mod, head = moss_ref.time_vecs(968.0, lambda n: wtime[n])
+    np.savez_compressed(os.path.join(HERE, "moss_text.npz"), T=Tt, text_seed=21, time_seed=22, t_code=968.0,
+                        x=xt.numpy(), txt=txt.numpy(), sin=s_t.numpy(), cos=c_t.numpy(), text_block=tb.numpy(),
+                        text_refine=tr.numpy(), mod=mod.numpy(), head=head.numpy())
     print("golden vectors written to", HERE)
 
 

@@ -175,3 +175,67 @@ def test_sigma_schedule_matches_animad():
     assert abs(float(sig[0]) - 1.0) < 1e-7 and float(sig[-1]) == 0.0
     s = np.linspace(1, 0.001, 4)
     np.testing.assert_allclose(np.array(sig[:4], np.float64), 3 * s / (1 + 2 * s), rtol=1e-6)
+
+
+# ---------------------------------------------------------------- MOSS text side and glue (moss_text.npz)
+@pytest.fixture(scope="module")
+def mtext():
+    return np.load(os.path.join(GOLD, "moss_text.npz"))
+
+
+def test_text_block_and_refine_match_moss_ref(mtext):
+    w = om.init_text_weights(int(mtext["text_seed"]), D=3072, F=256)
+    g = lambda n: w[n]
+    s, c = torch.from_numpy(mtext["sin"]), torch.from_numpy(mtext["cos"])
+    tb = om.text_block(torch.from_numpy(mtext["x"]), "text_embedder.blocks.0.", s, c, g)
+    tr = om.text_refine(torch.from_numpy(mtext["txt"]), s, c, g)
+    for got, want in ((tb, mtext["text_block"]), (tr, mtext["text_refine"])):
+        want = torch.from_numpy(want)
+        assert float((got - want).norm() / want.norm()) < 1e-5
+
+
+def test_time_vecs_match_moss_ref(mtext):
+    w = om.init_time_weights(int(mtext["time_seed"]), D=256)
+    mod, head = om.time_vecs(float(mtext["t_code"]), lambda n: w[n])
+    assert np.allclose(mod.numpy(), mtext["mod"], rtol=1e-5, atol=1e-6)
+    assert np.allclose(head.numpy(), mtext["head"], rtol=1e-5, atol=1e-6)
+
+
+def test_refiner_pack_mode1_form_matches_text_block():
+    """A refiner pack (biases in LoRA row 0) run in the device-operand form with the MODE 1 bias selector
+    equals text_block on the same dequantised weights."""
+    D, F, T = 3072, 256, 32
+    w = om.init_text_weights(31, D=D, F=F)
+    pack = om.build_refiner_pack(w, 0)
+    mats, gain = om.pack_mats(pack, D=D, F=F)
+    # the text_block weights as the pack holds them
+    ug = mats["ug"].view(F // 128, 2, 128, -1)
+    up, gate = ug[:, 0].reshape(F, -1), ug[:, 1].reshape(F, -1)
+    p = "text_embedder.blocks.0."
+    wd = {p + "qkv.weight": torch.cat([mats[n][:, :D] for n in "qkv"], 0),
+          p + "qkv.bias": torch.cat([mats[n][:, D] for n in "qkv"]),
+          p + "proj.weight": mats["o"][:, :D], p + "proj.bias": mats["o"][:, D],
+          p + "ffn_up.weight": up[:, :D], p + "ffn_up.bias": up[:, D],
+          p + "ffn_gate.weight": gate[:, :D], p + "ffn_gate.bias": gate[:, D],
+          p + "ffn_down.weight": mats["dn"][:, :F], p + "ffn_down.bias": mats["dn"][:, F],
+          p + "q_norm.weight": gain[:128] * np.sqrt(128.0), p + "k_norm.weight": gain[128:256],
+          p + "norm1.weight": gain[256:256 + D], p + "norm2.weight": gain[256 + D:256 + 2 * D]}
+    sin, cos = om.rope_tables(0, 1, T, om.bands16())
+    x = torch.randn(T, D, generator=torch.Generator().manual_seed(32))
+    ref = om.text_block(x, p, sin, cos, lambda n: wd[n])
+    mod = torch.zeros(6, D)
+    mod[2] = 1.0
+    mod[5] = 1.0
+    got = om.block_dev(x[None], mod, cos[:, :64], sin[:, :64], mats, gain, lora=True, refiner=True)[0]
+    assert float((got - ref).norm() / ref.norm()) < 1e-5
+
+
+def test_proj_pack_bias_row():
+    w = om.init_text_weights(33, D=3072, F=256, blocks=0)
+    pack = om.build_proj_pack(w)
+    assert len(pack) == 135397376
+    m = om.proj_mat(pack)
+    assert m.shape == (3072, 4224)
+    b = w["text_embedder.proj.bias"]
+    assert float((m[:, 4096] - b).abs().max()) < 1e-3 * float(b.abs().max())
+    assert float(m[:, 4097:].abs().max()) == 0.0
