@@ -59,6 +59,27 @@ struct Glue {
 };
 
 // Device scratch of the sampler, grown on demand (never inside a graph capture).
+struct MossGlue {
+  int D = 0;
+  __half *t_lin0 = nullptr, *t_lin2 = nullptr, *mod_w = nullptr, *head_w = nullptr, *fin_w = nullptr,
+         *emb = nullptr /* [D][192]: video_embedder with the bias in column 128 */;
+  float *t_b0 = nullptr, *t_b2 = nullptr, *mod_b = nullptr, *head_b = nullptr, *fin_norm = nullptr, *Q = nullptr;
+  std::vector<void*> owned;
+};
+constexpr int kMossEmbK = 192;  // 128 latent channels + the bias column, padded to the GEMM's K step
+
+// Device scratch of the MOSS sampler, grown on demand (never inside a graph capture).
+struct MossScratch {
+  int D = 0;
+  size_t rows = 0;
+  float *e = nullptr, *a = nullptr, *tm = nullptr, *mod = nullptr, *head = nullptr, *v = nullptr;
+  __half* xin = nullptr;
+  void release() {
+    for (void* p : {(void*)e, (void*)a, (void*)tm, (void*)mod, (void*)head, (void*)v, (void*)xin}) cudaFree(p);
+    *this = MossScratch();
+  }
+};
+
 struct SampleScratch {
   int S = 0, D = 0;
   size_t rows = 0;
@@ -96,6 +117,8 @@ struct hx_ctx {
   uint64_t graph_clock = 0;
   std::map<int, std::unique_ptr<Glue>> glues;
   SampleScratch ss;
+  std::map<int, std::unique_ptr<MossGlue>> moss_glues;
+  MossScratch ms;
   hx::SpState sp;
   std::mutex mu;
   void drop_graphs() {
@@ -659,15 +682,17 @@ int run_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, c
 // per-block modulation vectors in h->modscratch (allocated by the caller before any capture)
 constexpr size_t kModStride(int D) { return 9ull * D + 3 * 256; }
 
+// mods_dev: per-block device mod vectors, block k at mods_dev + k * mod_stride (stride 0: one shared vector,
+// as MOSS blocks use); NULL computes them from emb / lora with each block's AdaLN weights.
 int chain_body(hx_ctx* h, const std::vector<const Weights*>& ws, const int32_t* m, uint8_t* blob, const float* mods_dev,
-               const float* emb_dev, const float* lora_dev, uint32_t skipmask) {
+               const float* emb_dev, const float* lora_dev, uint32_t skipmask, size_t mod_stride) {
   const int model = ws[0]->model, D = ws[0]->D;
   const size_t per = model == HX_MODEL_ANIMA ? kModStride(D) : 6ull * D;
   for (size_t k = 0; k < ws.size(); ++k) {
     if ((skipmask >> k) & 1) continue;
     const float* md;
     if (mods_dev) {
-      md = mods_dev + k * (model == HX_MODEL_ANIMA ? 9ull * D : 6ull * D);
+      md = mods_dev + k * mod_stride;
     } else {
       float* out = h->modscratch + per * k;
       if (modulation_launch(ws[k]->modA, ws[k]->modB, emb_dev, lora_dev, out, 3, D, 256, 3 * D, h->stream) !=
@@ -775,7 +800,10 @@ int hx_close(hx_handle hh) {
     cudaFree(h->modscratch);
     for (auto& kv : h->glues)
       for (void* p : kv.second->owned) cudaFree(p);
+    for (auto& kv : h->moss_glues)
+      for (void* p : kv.second->owned) cudaFree(p);
     h->ss.release();
+    h->ms.release();
     cudaFree(h->status);
     for (auto& e : h->ev) cudaEventDestroy(e);
     if (h->own_stream) cudaStreamDestroy(h->stream);
@@ -1208,7 +1236,11 @@ int hx_chain(hx_handle hh, const int32_t* meta, int nmeta, const int* wfds, int 
                     reinterpret_cast<int64_t>(lora_dev), int64_t(skipmask)})
     key.push_back(v);
   const int r = run_graphed(
-      h, key, [&] { return chain_body(h, ws, m.data(), blob, mods_dev, emb_dev, lora_dev, skipmask); },
+      h, key,
+      [&] {
+        return chain_body(h, ws, m.data(), blob, mods_dev, emb_dev, lora_dev, skipmask,
+                          ws[0]->model == HX_MODEL_ANIMA ? 9ull * ws[0]->D : 6ull * ws[0]->D);
+      },
       use_graph != 0);
   return (*rc = r);
 }
@@ -1336,7 +1368,7 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
       ge.ldx = D;
       CKL(gemm_launch(ge, s));
       if (int r = chain_body(h, ws, m.data(), blob, nullptr, sc.emb + static_cast<size_t>(i) * D,
-                             sc.lora + static_cast<size_t>(i) * 3 * D, 0))
+                             sc.lora + static_cast<size_t>(i) * 3 * D, 0, 0))
         return r;
       const float* fm = sc.fmod + static_cast<size_t>(i) * 2 * D;
       CKL(lnmod_launch(x, hbuf, static_cast<int>(rows), D, fm, fm + D, 0, T, 1e-6f, s));
@@ -1356,6 +1388,160 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
   for (int i = 0; i <= nsteps; ++i) {
     int32_t bits;
     std::memcpy(&bits, &sig[i], 4);
+    key.push_back(bits);
+  }
+  return (*rc = run_graphed(h, key, body, use_graph != 0));
+}
+
+// ---------------------------------------------------------------- MOSS sampler
+int hx_moss_glue_load(hx_handle hh, const hx_moss_glue_desc* d, int* gfd) {
+  hx_ctx* h = H(hh);
+  if (!h || !d || !gfd || d->D <= 0 || d->D % 256) return HX_E_ARG;
+  if (!d->t_lin0 || !d->t_b0 || !d->t_lin2 || !d->t_b2 || !d->mod_w || !d->mod_b || !d->head_w || !d->head_b ||
+      !d->emb_w || !d->emb_b || !d->fin_norm || !d->fin_w || !d->mix_q)
+    return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  DevGuard g(h->device);
+  auto G = std::make_unique<MossGlue>();
+  const size_t D = d->D;
+  auto fail = [&](int r) {
+    cudaStreamSynchronize(h->stream);
+    for (void* p : G->owned) cudaFree(p);
+    return r;
+  };
+  auto copy = [&](const void* src, size_t bytes, void** dst) -> bool {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return false;
+    G->owned.push_back(p);
+    *dst = p;
+    return cudaMemcpyAsync(p, src, bytes, cudaMemcpyDeviceToDevice, h->stream) == cudaSuccess;
+  };
+  void* ptr[12] = {};
+  const bool ok = copy(d->t_lin0, D * 256 * 2, &ptr[0]) && copy(d->t_lin2, D * D * 2, &ptr[1]) &&
+                  copy(d->mod_w, 6 * D * D * 2, &ptr[2]) && copy(d->head_w, 2 * D * D * 2, &ptr[3]) &&
+                  copy(d->fin_w, 128 * D * 2, &ptr[4]) && copy(d->t_b0, D * 4, &ptr[5]) && copy(d->t_b2, D * 4, &ptr[6]) &&
+                  copy(d->mod_b, 6 * D * 4, &ptr[7]) && copy(d->head_b, 2 * D * 4, &ptr[8]) &&
+                  copy(d->fin_norm, D * 4, &ptr[9]) && copy(d->mix_q, 128 * 128 * 4, &ptr[10]);
+  if (!ok) return fail(HX_E_CUDA);
+  G->t_lin0 = static_cast<__half*>(ptr[0]);
+  G->t_lin2 = static_cast<__half*>(ptr[1]);
+  G->mod_w = static_cast<__half*>(ptr[2]);
+  G->head_w = static_cast<__half*>(ptr[3]);
+  G->fin_w = static_cast<__half*>(ptr[4]);
+  G->t_b0 = static_cast<float*>(ptr[5]);
+  G->t_b2 = static_cast<float*>(ptr[6]);
+  G->mod_b = static_cast<float*>(ptr[7]);
+  G->head_b = static_cast<float*>(ptr[8]);
+  G->fin_norm = static_cast<float*>(ptr[9]);
+  G->Q = static_cast<float*>(ptr[10]);
+  if (cudaMalloc(&ptr[11], D * kMossEmbK * 2) != cudaSuccess) return fail(HX_E_CUDA);
+  G->owned.push_back(ptr[11]);
+  G->emb = static_cast<__half*>(ptr[11]);
+  if (moss_emb_pad_launch(static_cast<const __half*>(d->emb_w), d->emb_b, G->emb, static_cast<int>(D), kMossEmbK,
+                          h->stream) != cudaSuccess ||
+      cudaStreamSynchronize(h->stream) != cudaSuccess)
+    return fail(HX_E_CUDA);
+  G->D = d->D;
+  *gfd = h->next_fd++;
+  h->moss_glues[*gfd] = std::move(G);
+  return HX_OK;
+}
+
+int hx_moss_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const int* wfds, int nblk, int bfd,
+                   const float* z, float* x0, int lat_h, int lat_w, const float* text, int ntext, int nsteps,
+                   const float* codes, int use_graph, int32_t* rc) {
+  hx_ctx* h = H(hh);
+  if (!h || !rc || !meta || !wfds || nblk <= 0 || !z || !x0 || !codes) return HX_E_ARG;
+  *rc = HX_OK;
+  if (nsteps <= 0 || nsteps > 8 || lat_h <= 0 || lat_w <= 0 || ntext < 0 || (ntext > 0 && !text))
+    return (*rc = HX_E_ARG);
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto gi = h->moss_glues.find(gfd);
+  if (gi == h->moss_glues.end()) return (*rc = HX_E_ARG);
+  const MossGlue& G = *gi->second;
+  auto bi = h->bufs.find(bfd);
+  if (bi == h->bufs.end()) return (*rc = HX_E_NOBLOB);
+  std::vector<const Weights*> ws(nblk);
+  for (int k = 0; k < nblk; ++k) {
+    auto wi = h->weights.find(wfds[k]);
+    if (wi == h->weights.end()) return (*rc = HX_E_NOWEIGHTS);
+    ws[k] = wi->second.get();
+    if (ws[k]->model != HX_MODEL_MOSS || ws[k]->proj || ws[k]->D != G.D) return (*rc = HX_E_ARG);
+  }
+  std::vector<int32_t> m = full_meta(meta, nmeta, HX_MODEL_MOSS);
+  const int D = G.D, ntok = m[HX_S_NTOK], B = m[HX_S_BATCH] > 0 ? m[HX_S_BATCH] : 1, Ni = lat_h * lat_w;
+  if (Ni + ntext > ntok || m[HX_S_SP] > 1) return (*rc = HX_E_ARG);
+  m[HX_S_NVALID] = Ni + ntext;
+  m[HX_S_MODE] = 0;
+  for (int k = 0; k < nblk; ++k)
+    if (int r = check_meta(*ws[k], m.data(), static_cast<int>(m.size()), bi->second.bytes)) return (*rc = r);
+  Sigmas cd{};
+  for (int i = 0; i < nsteps; ++i) cd.s[i] = codes[i];
+  DevGuard g(h->device);
+  const size_t rows = static_cast<size_t>(B) * ntok;
+  MossScratch& sc = h->ms;
+  if (sc.D != D || sc.rows < rows) {
+    cudaStreamSynchronize(h->stream);
+    h->drop_graphs();
+    sc.release();
+    const size_t S = 8;
+    bool ok = cudaMalloc(&sc.e, S * 256 * 4) == cudaSuccess && cudaMalloc(&sc.a, S * D * 4) == cudaSuccess &&
+              cudaMalloc(&sc.tm, S * D * 4) == cudaSuccess && cudaMalloc(&sc.mod, S * 6 * D * 4) == cudaSuccess &&
+              cudaMalloc(&sc.head, S * 2 * D * 4) == cudaSuccess && cudaMalloc(&sc.v, rows * 128 * 4) == cudaSuccess &&
+              cudaMalloc(&sc.xin, rows * kMossEmbK * 2) == cudaSuccess;
+    if (!ok) {
+      sc.release();
+      return (*rc = HX_E_CUDA);
+    }
+    sc.D = D;
+    sc.rows = rows;
+  }
+  uint8_t* blob = static_cast<uint8_t*>(bi->second.ptr);
+  float* x = reinterpret_cast<float*>(blob + m[HX_S_X]);
+  __half* hbuf = hptr(blob, m[HX_S_H]);
+  cudaStream_t s = h->stream;
+  auto body = [&]() -> int {
+    const int S = nsteps;
+    // time vectors of every step (moss_ref.py:96-105)
+    CKL(moss_temb_launch(cd, S, sc.e, s));
+    CKL(gemv_rows_launch(G.t_lin0, sc.e, sc.a, S, 256, D, 0, G.t_b0, 0, D, s));
+    CKL(gemv_rows_launch(G.t_lin2, sc.a, sc.tm, S, D, D, 1, G.t_b2, 0, D, s));
+    CKL(gemv_rows_launch(G.mod_w, sc.tm, sc.mod, S, D, 6 * D, 0, G.mod_b, 0, 6 * D, s));
+    CKL(gemv_rows_launch(G.head_w, sc.tm, sc.head, S, D, 2 * D, 0, G.head_b, 0, 2 * D, s));
+    DevMat we, wf;
+    we.fmt = WF_F16; we.N = D; we.K = kMossEmbK; we.w = G.emb;
+    wf.fmt = WF_F16; wf.N = 128; wf.K = D; wf.w = G.fin_w;
+    for (int i = 0; i < S; ++i) {
+      // rows = [video_embedder(z + Q x0) ; text ; 0]
+      CKL(moss_mix_launch(z, x0, G.Q, sc.xin, B, Ni, ntok, kMossEmbK, s));
+      GemmArgs ge = gargs(h, sc.xin, kMossEmbK, static_cast<int>(rows), &we, EPI_STORE32);
+      ge.x = x;
+      ge.ldx = D;
+      CKL(gemm_launch(ge, s));
+      for (int b = 0; b < B && ntext > 0; ++b)
+        CKL(cudaMemcpyAsync(x + (static_cast<size_t>(b) * ntok + Ni) * D, text, static_cast<size_t>(ntext) * D * 4,
+                            cudaMemcpyDeviceToDevice, s));
+      if (int r = chain_body(h, ws, m.data(), blob, sc.mod + static_cast<size_t>(i) * 6 * D, nullptr, nullptr, 0, 0))
+        return r;
+      // v = final_linear(rms(x) * norm * (1 + head1) + head0), x0 = z - v
+      const float* hd = sc.head + static_cast<size_t>(i) * 2 * D;
+      CKL(rmsmod_launch(x, hbuf, static_cast<int>(rows), D, G.fin_norm, hd, hd + D, 0, ntok, 1e-6f, s));
+      GemmArgs gf = gargs(h, hbuf, D, static_cast<int>(rows), &wf, EPI_STORE32);
+      gf.x = sc.v;
+      gf.ldx = 128;
+      CKL(gemm_launch(gf, s));
+      CKL(moss_x0_launch(z, sc.v, x0, B, Ni, ntok, 128, s));
+    }
+    return HX_OK;
+  };
+  std::vector<int64_t> key(m.begin(), m.end());
+  for (int k = 0; k < nblk; ++k) key.push_back(wfds[k]);
+  for (int64_t v : {int64_t(3), int64_t(gfd), int64_t(bfd), reinterpret_cast<int64_t>(z), reinterpret_cast<int64_t>(x0),
+                    reinterpret_cast<int64_t>(text), int64_t(lat_h), int64_t(lat_w), int64_t(ntext), int64_t(nsteps)})
+    key.push_back(v);
+  for (int i = 0; i < nsteps; ++i) {
+    int32_t bits;
+    std::memcpy(&bits, &codes[i], 4);
     key.push_back(bits);
   }
   return (*rc = run_graphed(h, key, body, use_graph != 0));

@@ -1,5 +1,7 @@
 // Per-step glue of the Anima sampler on the GPU (phone/animad.cpp:423-492): timestep embedding,
 // t_embedder mat-vecs, patchify, final-layer modulation, unpatchify and the Euler update.
+// MOSS sampler glue (moss/sample_ref.py:14-20, moss_ref.py:96-120, mossrun.cpp:306-333): the time
+// embedding of the step codes, the latent mix z + Q x0 feeding video_embedder, and x0 = z - v.
 // The GEMMs of the glue (x_embedder 68->D, final linear D->64) run on gemm.cu with an fp32-store
 // epilogue; the final LayerNorm modulation reuses elem.cu's lnmod.
 #include "hx_internal.h"
@@ -133,6 +135,67 @@ __global__ void pad_cols_kernel(const __half* __restrict__ src, __half* __restri
 
 }  // namespace
 
+// MOSS time embedding (moss_ref.py:97-100): e[s] = [cos(c_s f_i), sin(c_s f_i)], f_i = 10000^(-i/128),
+// computed in float64 and rounded once to float32 like the reference.
+__global__ void moss_temb_kernel(Sigmas codes, float* __restrict__ e) {
+  const int s = blockIdx.x, i = threadIdx.x;  // 256 threads
+  const int j = i & 127;
+  const double ph = static_cast<double>(codes.s[s]) * pow(10000.0, -static_cast<double>(j) / 128.0);
+  e[s * 256 + i] = static_cast<float>(i < 128 ? cos(ph) : sin(ph));
+}
+
+// xin[b][t][:] (fp16, row pitch kp) for the video_embedder GEMM: for image tokens t < Ni the mixed latent
+// z[b][o][t] + sum_c Q[o][c] x0[b][c][t] (sample_ref.py:16) in columns 0..127 and 1.0 in column 128 (the
+// embedder bias rides in the weight's column 128); text and padding rows t >= Ni are all zero.
+// One CTA per (32 tokens, image), thread o = output channel; Q^T and the x0 tile staged in shared memory.
+__global__ void __launch_bounds__(128) moss_mix_kernel(const float* __restrict__ z, const float* __restrict__ x0,
+                                                       const float* __restrict__ Q, __half* __restrict__ xin,
+                                                       int Ni, int ntok, int kp) {
+  extern __shared__ float sm[];
+  float* qt = sm;               // [128 c][128 o]
+  float* xs = sm + 128 * 128;   // [128 c][33]
+  const int b = blockIdx.y, t0 = blockIdx.x * 32, o = threadIdx.x;
+  for (int i = threadIdx.x; i < 128 * 128; i += blockDim.x) qt[(i % 128) * 128 + i / 128] = Q[i];
+  for (int i = threadIdx.x; i < 128 * 32; i += blockDim.x) {
+    const int c = i / 32, tt = i % 32;
+    xs[c * 33 + tt] = t0 + tt < Ni ? x0[(static_cast<size_t>(b) * 128 + c) * Ni + t0 + tt] : 0.f;
+  }
+  __syncthreads();
+  for (int tt = 0; tt < 32; ++tt) {
+    const int t = t0 + tt;
+    if (t >= ntok) break;
+    __half* row = xin + (static_cast<size_t>(b) * ntok + t) * kp;
+    if (t < Ni) {
+      float acc = 0.f;
+#pragma unroll 8
+      for (int c = 0; c < 128; ++c) acc = fmaf(qt[c * 128 + o], xs[c * 33 + tt], acc);
+      row[o] = __float2half_rn(z[(static_cast<size_t>(b) * 128 + o) * Ni + t] + acc);
+      for (int c = 128 + o; c < kp; c += 128) row[c] = __float2half_rn(c == 128 ? 1.f : 0.f);
+    } else {
+      for (int c = o; c < kp; c += 128) row[c] = __float2half_rn(0.f);
+    }
+  }
+}
+
+// x0[b][c][t] = z[b][c][t] - v[b*ntok + t][c]   (sample_ref.py:19), t < Ni
+__global__ void moss_x0_kernel(const float* __restrict__ z, const float* __restrict__ v, float* __restrict__ x0,
+                               int B, int Ni, int ntok, int ldv) {
+  const long total = static_cast<long>(B) * 128 * Ni;
+  const long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int t = static_cast<int>(i % Ni), c = static_cast<int>((i / Ni) % 128), b = static_cast<int>(i / (128L * Ni));
+  x0[i] = z[i] - v[(static_cast<size_t>(b) * ntok + t) * ldv + c];
+}
+
+// video_embedder W [D][128] fp16 + bias [D] fp32 -> [D][kp] fp16 with the bias in column 128
+__global__ void moss_emb_pad_kernel(const __half* __restrict__ W, const float* __restrict__ bias,
+                                    __half* __restrict__ Wp, int D, int kp) {
+  const long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long>(D) * kp) return;
+  const int r = static_cast<int>(i / kp), c = static_cast<int>(i % kp);
+  Wp[i] = c < 128 ? W[static_cast<size_t>(r) * 128 + c] : __float2half_rn(c == 128 ? bias[r] : 0.f);
+}
+
 cudaError_t pad_cols_launch(const __half* src, __half* dst, int rows, int cols, int ld_dst, cudaStream_t s) {
   const long total = static_cast<long>(rows) * ld_dst;
   pad_cols_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(src, dst, rows, cols, ld_dst);
@@ -169,6 +232,42 @@ cudaError_t unpatch_euler_launch(const float* y, float* lat, int B, int C, int H
                                  cudaStream_t s) {
   const long total = static_cast<long>(B) * C * H * W;
   unpatch_euler_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(y, lat, B, C, H, W, ldy, dt);
+  return cudaGetLastError();
+}
+
+cudaError_t moss_temb_launch(Sigmas codes, int S, float* e, cudaStream_t s) {
+  if (S <= 0 || S > 8) return cudaErrorInvalidValue;
+  moss_temb_kernel<<<S, 256, 0, s>>>(codes, e);
+  return cudaGetLastError();
+}
+
+cudaError_t moss_mix_launch(const float* z, const float* x0, const float* Q, __half* xin, int B, int Ni, int ntok,
+                            int kp, cudaStream_t s) {
+  if (B <= 0 || Ni <= 0 || ntok < Ni || kp < 129 || kp % 8) return cudaErrorInvalidValue;
+  constexpr int smem = (128 * 128 + 128 * 33) * 4;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1)) {
+    cudaError_t e = cudaFuncSetAttribute(moss_mix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set |= 1ull << dev;
+  }
+  dim3 grid((ntok + 31) / 32, B);
+  moss_mix_kernel<<<grid, 128, smem, s>>>(z, x0, Q, xin, Ni, ntok, kp);
+  return cudaGetLastError();
+}
+
+cudaError_t moss_x0_launch(const float* z, const float* v, float* x0, int B, int Ni, int ntok, int ldv,
+                           cudaStream_t s) {
+  const long total = static_cast<long>(B) * 128 * Ni;
+  moss_x0_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(z, v, x0, B, Ni, ntok, ldv);
+  return cudaGetLastError();
+}
+
+cudaError_t moss_emb_pad_launch(const __half* W, const float* bias, __half* Wp, int D, int kp, cudaStream_t s) {
+  const long total = static_cast<long>(D) * kp;
+  moss_emb_pad_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(W, bias, Wp, D, kp);
   return cudaGetLastError();
 }
 

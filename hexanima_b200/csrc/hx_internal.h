@@ -100,6 +100,13 @@ cudaError_t patchify_launch(const float* lat, __half* P, int B, int C, int H, in
 cudaError_t unpatch_euler_launch(const float* y, float* lat, int B, int C, int H, int W, int ldy, float dt,
                                  cudaStream_t s);
 cudaError_t pad_cols_launch(const __half* src, __half* dst, int rows, int cols, int ld_dst, cudaStream_t s);
+// MOSS sampler glue (glue.cu)
+cudaError_t moss_temb_launch(Sigmas codes, int S, float* e, cudaStream_t s);
+cudaError_t moss_mix_launch(const float* z, const float* x0, const float* Q, __half* xin, int B, int Ni, int ntok,
+                            int kp, cudaStream_t s);
+cudaError_t moss_x0_launch(const float* z, const float* v, float* x0, int B, int Ni, int ntok, int ldv,
+                           cudaStream_t s);
+cudaError_t moss_emb_pad_launch(const __half* W, const float* bias, __half* Wp, int D, int kp, cudaStream_t s);
 
 // weight repacking from the reference pack records (repack.cu)
 cudaError_t repack_tiles_launch(const uint8_t* rec, int nb, int kb, bool q8, void* dst, __half* scale, int row0,

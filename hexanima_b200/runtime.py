@@ -78,6 +78,12 @@ class hx_anima_glue_desc(ctypes.Structure):
                 ("f_modB", ctypes.c_void_p), ("f_lin", ctypes.c_void_p)]
 
 
+class hx_moss_glue_desc(ctypes.Structure):
+    _fields_ = [("D", ctypes.c_int)] + [(n, ctypes.c_void_p) for n in (
+        "t_lin0", "t_b0", "t_lin2", "t_b2", "mod_w", "mod_b", "head_w", "head_b", "emb_w", "emb_b", "fin_norm",
+        "fin_w", "mix_q")]
+
+
 class hx_gemm_desc(ctypes.Structure):
     _fields_ = [("a", ctypes.c_void_p), ("lda", ctypes.c_int), ("a2", ctypes.c_void_p), ("lda2", ctypes.c_int),
                 ("m", ctypes.c_int), ("k1", ctypes.c_int), ("w", hx_mat), ("epi", ctypes.c_int),
@@ -127,6 +133,8 @@ _SIGS = {
     "hx_chain": [_vp, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _vp, _vp, ctypes.c_uint32, _i, _ip],
     "hx_glue_load": [_vp, ctypes.POINTER(hx_anima_glue_desc), ctypes.POINTER(_i)],
     "hx_anima_sample": [_vp, _i, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _i, _i, _i, _vp, _i, _ip],
+    "hx_moss_glue_load": [_vp, ctypes.POINTER(hx_moss_glue_desc), ctypes.POINTER(_i)],
+    "hx_moss_sample": [_vp, _i, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _ip],
     "hx_gemm": [_vp, ctypes.POINTER(hx_gemm_desc)],
     "hx_attention": [_vp, ctypes.POINTER(hx_attn_desc)],
     "hx_lnmod": [_vp, _vp, _vp, _i, _i, _vp, _vp, _l, _i, _f],
@@ -352,6 +360,26 @@ class Handle:
         _check(rc.value, "hx_anima_sample rc")
 
     # -------------------------------------------------------------- operators
+    def moss_glue_load(self, D, **arrays):
+        """MOSS sampler glue from device arrays named as the hx_moss_glue_desc fields (copied by the library)."""
+        d = hx_moss_glue_desc()
+        d.D = D
+        for name, _ in hx_moss_glue_desc._fields_[1:]:
+            setattr(d, name, _ptr(arrays[name]))
+        gfd = ctypes.c_int()
+        _check(lib().hx_moss_glue_load(self.h, ctypes.byref(d), ctypes.byref(gfd)), "hx_moss_glue_load")
+        return gfd.value
+
+    def moss_sample(self, gfd, meta, wfds, bfd, z_dev, x0_dev, lat_h, lat_w, text_dev, ntext, codes, use_graph=True):
+        m = (ctypes.c_int32 * len(meta))(*meta)
+        w = (ctypes.c_int * len(wfds))(*wfds)
+        c = np.ascontiguousarray(codes, np.float32)
+        rc = ctypes.c_int32()
+        r = lib().hx_moss_sample(self.h, gfd, m, len(meta), w, len(wfds), bfd, _ptr(z_dev), _ptr(x0_dev), lat_h, lat_w,
+                                 _ptr(text_dev), ntext, len(c), c.ctypes.data, 1 if use_graph else 0, ctypes.byref(rc))
+        _check(r, "hx_moss_sample")
+        _check(rc.value, "hx_moss_sample rc")
+
     def gemm(self, a, m, mat, epi=EPI_STORE, lda=None, k1=0, a2=None, lda2=0, out=None, ldo=0, x=None, ldx=0,
              gate=None, vec_bstride=0, rows_per_img=0, gain0=None, gain1=None, seg1=0, seg2=0, rope0=0, rope1=0,
              cos_t=None, sin_t=None, eps=1e-6, tile=0):

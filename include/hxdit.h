@@ -263,6 +263,37 @@ HX_API int hx_anima_sample(hx_handle h, int gfd, const int32_t* meta, int nmeta,
                            float* latent_dev, int lat_h, int lat_w, int nsteps, const float* sigmas, int use_graph,
                            int32_t* rc);
 
+/* MOSS sampler glue (moss/sample_ref.py:14-20 with moss_ref.py:96-120 dit_forward; mossrun.cpp:306-333):
+ * weights as device arrays (copied), fp16 matrices and fp32 vectors, moss_ref names. */
+typedef struct {
+  int D;                  /* 3072 (a multiple of 256) */
+  const void* t_lin0;     /* fp16 [D][256]   time_embedding.0.weight */
+  const float* t_b0;      /* fp32 [D]        time_embedding.0.bias */
+  const void* t_lin2;     /* fp16 [D][D]     time_embedding.2.weight */
+  const float* t_b2;      /* fp32 [D]        time_embedding.2.bias */
+  const void* mod_w;      /* fp16 [6D][D]    shared_block_modulation.weight */
+  const float* mod_b;     /* fp32 [6D] */
+  const void* head_w;     /* fp16 [2D][D]    video_head_modulation.weight */
+  const float* head_b;    /* fp32 [2D] */
+  const void* emb_w;      /* fp16 [D][128]   video_embedder.weight */
+  const float* emb_b;     /* fp32 [D]        (rounded to fp16: it rides in the GEMM's K column 128) */
+  const float* fin_norm;  /* fp32 [D]        final_norm_video.weight */
+  const void* fin_w;      /* fp16 [128][D]   final_linear_video.weight */
+  const float* mix_q;     /* fp32 [128][128] latent_mix.Q */
+} hx_moss_glue_desc;
+HX_API int hx_moss_glue_load(hx_handle h, const hx_moss_glue_desc* desc, int* gfd);
+/* A MOSS sample over nsteps <= 8 step codes (host floats, e.g. 1000 968 926 871): per step
+ *   xin = z + Q x0;  rows = [video_embedder(xin) ; text rows];  mod, head = time vectors(code);
+ *   nblk blocks (MODE 0, one shared mod);  v = final_linear(rms(x) * fin_norm * (1 + head1) + head0);  x0 = z - v.
+ * z_dev, x0_dev: fp32 [B][128][lat_h][lat_w] (x0 in/out: zeros for a fresh sample, the clean estimate at
+ * the end); text_dev: fp32 [ntext][D] refined text rows, shared by the B = meta BATCH images. meta: a MOSS
+ * blob layout with NTOK >= lat_h*lat_w + ntext; NVALID is set to lat_h*lat_w + ntext; the caller fills
+ * COS/SIN with hx_rope_moss(lat_h, lat_w, ntext, bands, NTOK). The whole sample runs as one CUDA graph
+ * when use_graph != 0. */
+HX_API int hx_moss_sample(hx_handle h, int gfd, const int32_t* meta, int nmeta, const int* wfds, int nblk, int bfd,
+                          const float* z_dev, float* x0_dev, int lat_h, int lat_w, const float* text_dev, int ntext,
+                          int nsteps, const float* codes, int use_graph, int32_t* rc);
+
 /* ------------------------------------------------------------------ operator level (device pointers) */
 typedef struct {
   const void* a; int lda;       /* fp16 [m][lda], columns [0,k1) */

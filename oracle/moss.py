@@ -320,3 +320,42 @@ def proj_mat(pack, D=3072, TW=4096):
     size = (D // 32) * ((TW + 128) // 32) * 1152
     w = dequant_q8_f16(pack[:size], D // 32, (TW + 128) // 32).astype(np.float32)   # [K][N]
     return torch.from_numpy(np.ascontiguousarray(w.T))
+
+
+def sample_dev(z, x0, tx, glue, blocks, codes, cos64, sin64, ntok):
+    """MOSS sampler in device-operand form: sample_ref.py:15-20 around moss_ref.dit_forward (moss_ref.py:
+    107-120) with the text rows `tx` already refined. z, x0 [B, 128, Ni]; tx [T, D]; glue: moss_ref-named
+    tensors holding the values the device multiplies (fp16-rounded matrices; video_embedder.bias rounded to
+    fp16 because it rides in the embedder GEMM's K column); blocks: [(mats, gain, lora)] for block_dev.
+    The embedder input and the final-layer input are rounded to fp16 as the device GEMMs take them."""
+    B, C, Ni = z.shape
+    T, D = tx.shape
+    g = lambda n: glue[n]
+    for code in codes:
+        xin = z + torch.einsum("oc,bct->bot", g("latent_mix.Q"), x0)
+        rows = xin.transpose(1, 2).half().float() @ g("video_embedder.weight").T + g("video_embedder.bias")
+        x = torch.zeros(B, ntok, D)
+        x[:, :Ni] = rows
+        x[:, Ni:Ni + T] = tx
+        mod, head = time_vecs(code, g)
+        for mats, gain, lora in blocks:
+            x = block_dev(x, mod, cos64, sin64, mats, gain, nvalid=Ni + T, lora=lora)
+        hf = (rms(x, g("final_norm_video.weight")) * (1 + head[1]) + head[0]).half().float()
+        v = (hf @ g("final_linear_video.weight").T)[:, :Ni]           # [B, Ni, 128]
+        x0 = z - v.transpose(1, 2)
+    return x0
+
+
+def init_glue_weights(seed, D, std=0.02):
+    """Seeded synthetic sampler glue (moss_ref names), matrices already fp16-rounded as the device holds them."""
+    w = init_time_weights(seed, D=D, std=std)
+    gen = torch.Generator().manual_seed(seed + 1)
+    n = lambda *s: torch.randn(*s, generator=gen) * std
+    w.update({"video_embedder.weight": n(D, 128) * 5, "video_embedder.bias": n(D),
+              "final_norm_video.weight": 1 + n(D), "final_linear_video.weight": n(128, D),
+              "latent_mix.Q": n(128, 128) * 10})
+    for k in ("time_embedding.0.weight", "time_embedding.2.weight", "shared_block_modulation.weight",
+              "video_head_modulation.weight", "video_embedder.weight", "video_embedder.bias",
+              "final_linear_video.weight"):
+        w[k] = w[k].half().float()
+    return w
