@@ -1447,6 +1447,149 @@ int hx_moss_glue_load(hx_handle hh, const hx_moss_glue_desc* d, int* gfd) {
   return HX_OK;
 }
 
+namespace {
+struct Mgl1Entry {
+  char name[41];
+  int32_t dtype, nd, dims[3];
+  int64_t off, bytes;
+};
+// parse and validate every entry of an MGL1 file (export_glue.py layout, little endian, 76-byte entries)
+int mgl1_entries(const uint8_t* b, size_t size, std::vector<Mgl1Entry>& out) {
+  constexpr size_t kEnt = 40 + 4 + 4 + 12 + 8 + 8;
+  if (!b || size < 8 || std::memcmp(b, "MGL1", 4) != 0) return HX_E_FORMAT;
+  int32_t n;
+  std::memcpy(&n, b + 4, 4);
+  if (n < 0 || static_cast<size_t>(n) > (size - 8) / kEnt) return HX_E_FORMAT;
+  out.resize(n);
+  for (int i = 0; i < n; ++i) {
+    const uint8_t* e = b + 8 + static_cast<size_t>(i) * kEnt;
+    Mgl1Entry& m = out[i];
+    std::memcpy(m.name, e, 40);
+    m.name[40] = 0;
+    std::memcpy(&m.dtype, e + 40, 4);
+    std::memcpy(&m.nd, e + 44, 4);
+    std::memcpy(m.dims, e + 48, 12);
+    std::memcpy(&m.off, e + 60, 8);
+    std::memcpy(&m.bytes, e + 68, 8);
+    if ((m.dtype != 0 && m.dtype != 1) || m.nd < 0 || m.nd > 3 || m.off < 0 || m.bytes < 0) return HX_E_FORMAT;
+    if (static_cast<uint64_t>(m.off) > size || static_cast<uint64_t>(m.bytes) > size - m.off) return HX_E_FORMAT;
+    int64_t elems = 1;
+    for (int d = 0; d < 3; ++d) {
+      if (m.dims[d] < 0) return HX_E_FORMAT;
+      elems *= m.dims[d];
+    }
+    if (elems * (m.dtype ? 2 : 4) != m.bytes) return HX_E_FORMAT;
+  }
+  return HX_OK;
+}
+}  // namespace
+
+int hx_mgl1_tensor(const void* file, size_t bytes, const char* name, int* dtype, int* nd, int32_t dims[3],
+                   const void** data, size_t* nbytes) {
+  if (!name) return HX_E_ARG;
+  std::vector<Mgl1Entry> es;
+  if (int r = mgl1_entries(static_cast<const uint8_t*>(file), bytes, es)) return r;
+  for (const Mgl1Entry& e : es) {
+    if (std::strncmp(e.name, name, 40) != 0) continue;
+    if (dtype) *dtype = e.dtype;
+    if (nd) *nd = e.nd;
+    if (dims) std::memcpy(dims, e.dims, 12);
+    if (data) *data = static_cast<const uint8_t*>(file) + e.off;
+    if (nbytes) *nbytes = static_cast<size_t>(e.bytes);
+    return HX_OK;
+  }
+  return HX_E_RANGE;
+}
+
+int hx_moss_glue_load_mgl1(hx_handle hh, const void* file, size_t bytes, int* gfd) {
+  hx_ctx* h = H(hh);
+  if (!h || !file || !gfd) return HX_E_ARG;
+  std::vector<Mgl1Entry> es;
+  if (int r = mgl1_entries(static_cast<const uint8_t*>(file), bytes, es)) return r;
+  const uint8_t* base = static_cast<const uint8_t*>(file);
+  auto find = [&](const char* n) -> const Mgl1Entry* {
+    for (const Mgl1Entry& e : es)
+      if (std::strncmp(e.name, n, 40) == 0) return &e;
+    return nullptr;
+  };
+  const Mgl1Entry* emb = find("video_embedder.weight");
+  if (!emb || emb->nd != 2) return HX_E_FORMAT;
+  const int64_t D = emb->dims[0];
+  // name, rows, cols (cols 1 for vectors), device dtype (1 fp16, 0 fp32)
+  struct Need { const char* name; int64_t r, c; int f16; };
+  const Need need[13] = {{"time_embedding.0.weight", D, 256, 1}, {"time_embedding.0.bias", D, 1, 0},
+                         {"time_embedding.2.weight", D, D, 1},  {"time_embedding.2.bias", D, 1, 0},
+                         {"shared_block_modulation.weight", 6 * D, D, 1}, {"shared_block_modulation.bias", 6 * D, 1, 0},
+                         {"video_head_modulation.weight", 2 * D, D, 1}, {"video_head_modulation.bias", 2 * D, 1, 0},
+                         {"video_embedder.weight", D, 128, 1},  {"video_embedder.bias", D, 1, 0},
+                         {"final_norm_video.weight", D, 1, 0},  {"final_linear_video.weight", 128, D, 1},
+                         {"latent_mix.Q", 128, 128, 0}};
+  std::vector<void*> tmp;
+  auto cleanup = [&](int r) {
+    for (void* p : tmp) cudaFree(p);
+    return r;
+  };
+  void* dptr[13] = {};
+  for (int i = 0; i < 13; ++i) {
+    const Mgl1Entry* e = find(need[i].name);
+    if (!e) return cleanup(HX_E_FORMAT);
+    const int64_t n = need[i].r * need[i].c;
+    if (static_cast<int64_t>(e->dims[0]) * std::max(1, e->dims[1]) * std::max(1, e->dims[2]) != n) return cleanup(HX_E_FORMAT);
+    std::vector<uint16_t> h16;
+    std::vector<float> f32;
+    const void* src = base + e->off;
+    size_t nb;
+    if (need[i].f16) {
+      if (e->dtype == 1) {
+        nb = n * 2;
+      } else {
+        h16.resize(n);
+        for (int64_t k = 0; k < n; ++k) {
+          float v;
+          std::memcpy(&v, base + e->off + 4 * k, 4);
+          h16[k] = __half_as_ushort(__float2half_rn(v));
+        }
+        src = h16.data();
+        nb = n * 2;
+      }
+    } else {
+      if (e->dtype == 0) {
+        nb = n * 4;
+      } else {
+        f32.resize(n);
+        for (int64_t k = 0; k < n; ++k) {
+          uint16_t u;
+          std::memcpy(&u, base + e->off + 2 * k, 2);
+          f32[k] = __half2float(__ushort_as_half(u));
+        }
+        src = f32.data();
+        nb = n * 4;
+      }
+    }
+    DevGuard g(h->device);
+    if (cudaMalloc(&dptr[i], nb) != cudaSuccess) return cleanup(HX_E_CUDA);
+    tmp.push_back(dptr[i]);
+    if (cudaMemcpy(dptr[i], src, nb, cudaMemcpyHostToDevice) != cudaSuccess) return cleanup(HX_E_CUDA);
+  }
+  hx_moss_glue_desc d;
+  d.D = static_cast<int>(D);
+  d.t_lin0 = dptr[0];
+  d.t_b0 = static_cast<const float*>(dptr[1]);
+  d.t_lin2 = dptr[2];
+  d.t_b2 = static_cast<const float*>(dptr[3]);
+  d.mod_w = dptr[4];
+  d.mod_b = static_cast<const float*>(dptr[5]);
+  d.head_w = dptr[6];
+  d.head_b = static_cast<const float*>(dptr[7]);
+  d.emb_w = dptr[8];
+  d.emb_b = static_cast<const float*>(dptr[9]);
+  d.fin_norm = static_cast<const float*>(dptr[10]);
+  d.fin_w = dptr[11];
+  d.mix_q = static_cast<const float*>(dptr[12]);
+  const int r = hx_moss_glue_load(hh, &d, gfd);
+  return cleanup(r);
+}
+
 int hx_moss_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const int* wfds, int nblk, int bfd,
                    const float* z, float* x0, int lat_h, int lat_w, const float* text, int ntext, int nsteps,
                    const float* codes, int use_graph, int32_t* rc) {

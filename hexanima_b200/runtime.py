@@ -134,6 +134,9 @@ _SIGS = {
     "hx_glue_load": [_vp, ctypes.POINTER(hx_anima_glue_desc), ctypes.POINTER(_i)],
     "hx_anima_sample": [_vp, _i, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _i, _i, _i, _vp, _i, _ip],
     "hx_moss_glue_load": [_vp, ctypes.POINTER(hx_moss_glue_desc), ctypes.POINTER(_i)],
+    "hx_mgl1_tensor": [_vp, _sz, ctypes.c_char_p, ctypes.POINTER(_i), ctypes.POINTER(_i), _ip, ctypes.POINTER(_vp),
+                       ctypes.POINTER(_sz)],
+    "hx_moss_glue_load_mgl1": [_vp, _vp, _sz, ctypes.POINTER(_i)],
     "hx_moss_sample": [_vp, _i, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _ip],
     "hx_gemm": [_vp, ctypes.POINTER(hx_gemm_desc)],
     "hx_attention": [_vp, ctypes.POINTER(hx_attn_desc)],
@@ -207,6 +210,18 @@ def pack_apply_overlay(pack, ovl):
     pb = (ctypes.c_char * len(pack)).from_buffer(pack)
     ob = ctypes.create_string_buffer(bytes(ovl), len(ovl))
     _check(lib().hx_pack_apply_overlay(ctypes.addressof(pb), len(pack), ob, len(ovl)), "hx_pack_apply_overlay")
+
+
+def mgl1_tensor(file_bytes, name):
+    """A tensor of an MGL1 glue file (bytes) as a numpy array (float32 or float16), via hx_mgl1_tensor."""
+    buf = ctypes.create_string_buffer(bytes(file_bytes), len(file_bytes))
+    dt, nd, dims = ctypes.c_int(), ctypes.c_int(), (ctypes.c_int32 * 3)()
+    data, nb = ctypes.c_void_p(), ctypes.c_size_t()
+    _check(lib().hx_mgl1_tensor(buf, len(file_bytes), name.encode(), ctypes.byref(dt), ctypes.byref(nd), dims,
+                                ctypes.byref(data), ctypes.byref(nb)), "hx_mgl1_tensor")
+    off = data.value - ctypes.addressof(buf)
+    a = np.frombuffer(bytes(file_bytes)[off:off + nb.value], np.float16 if dt.value else np.float32)
+    return a.reshape(list(dims)[:nd.value]).copy()
 
 
 def sp_unique_id():
@@ -368,6 +383,12 @@ class Handle:
             setattr(d, name, _ptr(arrays[name]))
         gfd = ctypes.c_int()
         _check(lib().hx_moss_glue_load(self.h, ctypes.byref(d), ctypes.byref(gfd)), "hx_moss_glue_load")
+        return gfd.value
+
+    def moss_glue_load_mgl1(self, file_bytes):
+        buf = ctypes.create_string_buffer(bytes(file_bytes), len(file_bytes))
+        gfd = ctypes.c_int()
+        _check(lib().hx_moss_glue_load_mgl1(self.h, buf, len(file_bytes), ctypes.byref(gfd)), "hx_moss_glue_load_mgl1")
         return gfd.value
 
     def moss_sample(self, gfd, meta, wfds, bfd, z_dev, x0_dev, lat_h, lat_w, text_dev, ntext, codes, use_graph=True):

@@ -282,6 +282,15 @@ typedef struct {
   const float* mix_q;     /* fp32 [128][128] latent_mix.Q */
 } hx_moss_glue_desc;
 HX_API int hx_moss_glue_load(hx_handle h, const hx_moss_glue_desc* desc, int* gfd);
+/* MOSS glue file glue.bin (moss/export_glue.py:1-2,17-23): "MGL1", int32 n, n entries of
+ * {char name[40]; int32 dtype (0 f32, 1 f16); int32 nd; int32 dims[3]; int64 offset; int64 bytes}, data
+ * 128-byte aligned. hx_mgl1_tensor finds a tensor by name in the file bytes (host memory): HX_E_FORMAT
+ * for a malformed file, HX_E_RANGE if the name is absent. hx_moss_glue_load_mgl1 builds the sampler glue
+ * from such a file (fp32 matrices rounded to fp16 for the device mat-vecs and GEMMs); step_codes and
+ * rope.bands stay with the caller (read them with hx_mgl1_tensor). */
+HX_API int hx_mgl1_tensor(const void* file, size_t bytes, const char* name, int* dtype, int* nd, int32_t dims[3],
+                          const void** data, size_t* nbytes);
+HX_API int hx_moss_glue_load_mgl1(hx_handle h, const void* file, size_t bytes, int* gfd);
 /* A MOSS sample over nsteps <= 8 step codes (host floats, e.g. 1000 968 926 871): per step
  *   xin = z + Q x0;  rows = [video_embedder(xin) ; text rows];  mod, head = time vectors(code);
  *   nblk blocks (MODE 0, one shared mod);  v = final_linear(rms(x) * fin_norm * (1 + head1) + head0);  x0 = z - v.

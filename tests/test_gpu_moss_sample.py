@@ -83,6 +83,16 @@ def test_moss_sample_matches_oracle(h):
                         ntok)
     assert rel(results[0], ref) < 1e-2
     assert rel(results[0] - z, ref - z) < 1e-2          # the velocity part itself, not just z
+    # the same glue read from a glue.bin file (export_glue.py dtypes: fp32 except the two modulation matrices)
+    from tests.test_mgl1 import write_mgl1
+    f16 = ("shared_block_modulation.weight", "video_head_modulation.weight")
+    f = write_mgl1([(k, 1 if k in f16 else 0, v.numpy()) for k, v in glue.items()] +
+                   [("step_codes", 0, np.array(CODES, np.float32)), ("rope.bands", 0, om.bands16().numpy())])
+    gfd2 = h.moss_glue_load_mgl1(f)
+    x0d = torch.zeros(B, 128, Ni, device="cuda")
+    h.moss_sample(gfd2, meta, wfds, bfd, zd, x0d, LH, LW, txd, T, rt.mgl1_tensor(f, "step_codes"))
+    h.sync()
+    assert torch.equal(x0d.cpu(), results[0])
     h.buf_free(bfd)
     for w in wfds:
         h.weights_free(w)
