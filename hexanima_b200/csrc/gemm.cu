@@ -179,14 +179,45 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
         xr[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
                             __uint_as_float(r[4 * q + 3]));
     }
-  } else if constexpr (EPI == EPI_STORE || EPI == EPI_GELU || EPI == EPI_RESID) {
+  } else if constexpr (EPI == EPI_STORE || EPI == EPI_GELU) {
+    // fp16 out: 64 columns at a time staged in the 128-B swizzled stage, written by one TMA store
+    // (the tensor map clips rows >= M and columns >= N)
+    const int row = warp * 32 + lane;
+#pragma unroll 1
+    for (int g = 0; g < BN / 64; ++g) {
+      if (n0 + 64 * g >= p.N) break;  // uniform over the epilogue warps
+      if (threadIdx.x == 0) bulk_wait_read<0>();  // the previous group's store has read the stage
+      named_bar(1, EPI_WARPS * 32);
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        tmem_ld32(tl + 64 * g + 32 * h, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if constexpr (EPI == EPI_GELU) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          st_shared_v4(stage + row * 128 + (((4 * h + q) ^ (row & 7)) << 4), pack_half2(v[8 * q], v[8 * q + 1]),
+                       pack_half2(v[8 * q + 2], v[8 * q + 3]), pack_half2(v[8 * q + 4], v[8 * q + 5]),
+                       pack_half2(v[8 * q + 6], v[8 * q + 7]));
+      }
+      fence_proxy_async_smem();
+      named_bar(1, EPI_WARPS * 32);
+      if (threadIdx.x == 0) {
+        tma_store_2d(tmX, stage_ptr, n0 + 64 * g, m0);
+        bulk_commit();
+      }
+    }
+  } else if constexpr (EPI == EPI_RESID) {
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       const int n = n0 + 32 * c;
       if (n >= p.N) break;  // warp-uniform
       tmem_ld32(tl + 32 * c, r);
       tmem_ld_wait();
-      if (EPI != EPI_RESID && !row_ok) continue;
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
       if constexpr (EPI == EPI_RESID) {
@@ -209,12 +240,6 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
           tma_reduce_add_2d(tmX, stage_ptr, n, m0);
           bulk_commit();
         }
-      } else {
-        if constexpr (EPI == EPI_GELU) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-        }
-        store_row32_f16(p.out + static_cast<size_t>(m) * p.ldo + n, v);
       }
     }
   } else if constexpr (EPI == EPI_RMS) {
@@ -379,7 +404,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     prefetch_tmap(&tmW);
     if (p.nkb1 < p.nkb) prefetch_tmap(&tmA2);
     if (FMT != WF_F16) prefetch_tmap(&tmS);
-    if (EPI == EPI_RESID) prefetch_tmap(&tmX);
+    if (EPI == EPI_RESID || EPI == EPI_STORE || EPI == EPI_GELU) prefetch_tmap(&tmX);
   }
   tc_fence_before();
   __syncthreads();
@@ -488,8 +513,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
-    if constexpr (EPI == EPI_RESID) {
-      if (threadIdx.x == 0) bulk_wait<0>();  // reductions complete before the CTA's shared memory goes away
+    if constexpr (EPI == EPI_RESID || EPI == EPI_STORE || EPI == EPI_GELU) {
+      if (threadIdx.x == 0) bulk_wait<0>();  // stores / reductions complete before the shared memory goes away
     }
   }
 
@@ -583,7 +608,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     prefetch_tmap(&tmW);
     if (p.nkb1 < p.nkb) prefetch_tmap(&tmA2);
     if (FMT != WF_F16) prefetch_tmap(&tmS);
-    if (EPI == EPI_RESID) prefetch_tmap(&tmX);
+    if (EPI == EPI_RESID || EPI == EPI_STORE || EPI == EPI_GELU) prefetch_tmap(&tmX);
   }
   tc_fence_before();
   cluster_sync();  // barriers of both CTAs initialised, TMEM of the pair allocated
@@ -689,8 +714,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_leader(&tempty[acc]);
     }
-    if constexpr (EPI == EPI_RESID) {
-      if (threadIdx.x == 0) bulk_wait<0>();
+    if constexpr (EPI == EPI_RESID || EPI == EPI_STORE || EPI == EPI_GELU) {
+      if (threadIdx.x == 0) bulk_wait<0>();  // stores and reduce-adds of the last tile complete
     }
   }
 
@@ -846,6 +871,10 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   if (a.epi == EPI_RESID && (!a.x || !a.gate)) return cudaErrorInvalidValue;
   if (a.epi == EPI_STORE32 && (!a.x || a.ldx % 4)) return cudaErrorInvalidValue;
   if (a.epi != EPI_RESID && a.epi != EPI_STORE32 && !a.out) return cudaErrorInvalidValue;
+  // fp16 outputs are written 16 bytes at a time (and by TMA stores): 16-byte aligned rows
+  if (a.epi != EPI_RESID && a.epi != EPI_STORE32 &&
+      (a.ldo % 8 || reinterpret_cast<uintptr_t>(a.out) % 16 || a.ldo < (a.epi == EPI_SITU ? N / 2 : N)))
+    return cudaErrorInvalidValue;
   if (W->fmt == WF_Q8 && W->group != 32 && W->group != 64) return cudaErrorInvalidValue;
   if ((W->fmt == WF_Q4 || W->fmt == WF_Q4A) && W->group != 32) return cudaErrorInvalidValue;
 
@@ -863,6 +892,10 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   memset(&tX, 0, sizeof tX);
   if (a.epi == EPI_RESID &&
       !make_tmap_2d(&tX, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.x, N, a.M, static_cast<uint64_t>(a.ldx) * 4, 32, BM,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if ((a.epi == EPI_STORE || a.epi == EPI_GELU) &&
+      !make_tmap_2d(&tX, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.out, N, a.M, static_cast<uint64_t>(a.ldo) * 2, 64, BM,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   if (!make_tmap_2d(&tA, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.A, a.K1, a.M, static_cast<uint64_t>(a.lda) * 2, BK,

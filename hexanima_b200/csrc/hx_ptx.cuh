@@ -103,6 +103,14 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const 
       "r"(smem_u32(src)), "r"(x), "r"(y)
       : "memory");
 }
+// shared -> global tiled store (no multicast); rows / columns outside the tensor are not written
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // wait until at most N bulk groups still read their shared-memory sources
 template <int N>
