@@ -377,6 +377,8 @@ def main():
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    # NCCL prints its debug lines (the version line included) on stdout; stdout carries only the JSON line
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
