@@ -1,6 +1,6 @@
 """Benchmark: 512x768 4-step images/s of the Anima-2.9B-shaped q8 DiT.
 
-python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch 8]
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch 8] [--config 3|2]
 
 Workload (configs[2] of BASELINE.json): 36 blocks (hidden 2048, 16 heads x 128, 1536 image tokens =
 32x48 patches, cross-attention to 256 text tokens of width 1024, GELU MLP 8192), int8 weights in
@@ -9,6 +9,9 @@ groups of 64 along K with fp16 scales, 4 denoising steps, batch 8 images split o
 rank's images through hx_anima_sample (one CUDA graph): timestep embeddings, then per denoising step
 patchify + x_embedder, the AdaLN modulation and forward of all 36 blocks, final layer, unpatchify
 and the Euler update of the 16-channel 64x96 latent (animad.cpp:423-492 on the GPU).
+
+--config 2 (configs[1]: 28 blocks of fp16 weights, batch 1, the north_star's "< 40 ms per image"
+case) runs the same sample on one image per rank.
 
 Timing: CUDA events on the runtime's stream, barrier + synchronize around the K timed steps, max
 over ranks. The weights (2.8 GB) are far larger than L2 (126 MB), so every step streams them from
@@ -32,6 +35,7 @@ sys.path.insert(0, ROOT)
 
 D, HEADS, T, C, CD, F, NBLK, NSTEP = 2048, 16, 1536, 256, 1024, 8192, 36, 4
 GROUP = 64
+FMT = "q8"   # config 3 (the default); --config 2 switches to 28 fp16 blocks, batch 1
 GEMM_FLOP_BLOCK = 2 * T * (D * 3 * D + D * D * 3 + 2 * D * F) + 2 * C * CD * 2 * D   # per image
 ATTN_FLOP_BLOCK = 4 * T * T * D + 4 * T * C * D
 
@@ -153,10 +157,12 @@ def run_reference(args, rank, world):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": per_block * NBLK * NSTEP * 1e3, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "anima2.9b-q8-g64 512x768 4-step (config 3)", "blocks": NBLK, "steps": NSTEP,
-                       "tokens": T, "ctx": C, "sample": "1 block forward per step, 1 image, extrapolated x144"},
+            "config": {"workload": ("anima2b-f16 512x768 4-step (config 2)" if FMT == "f16"
+                                    else "anima2.9b-q8-g64 512x768 4-step (config 3)"), "blocks": NBLK,
+                       "steps": NSTEP, "tokens": T, "ctx": C,
+                       "sample": f"1 block forward per step, 1 image, extrapolated x{NBLK * NSTEP}"},
             "cpu_baseline": {"value": img_s, "unit": "images/s", "cores": threads, "kind": "port",
-                             "sample": "oracle Anima block (torch fp32) at T=1536, 1 image; images/s = 1/(t_block*36*4)"},
+                             "sample": f"oracle Anima block (torch fp32) at T=1536, 1 image; images/s = 1/(t_block*{NBLK}*4)"},
             "e2e": {"value": img_s, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -172,6 +178,11 @@ def synth_weights(h, rt, torch, dev, seed):
     for _ in range(NBLK):
         mats = {}
         for slot, (n, k) in shapes.items():
+            if FMT == "f16":   # config 2: fp16 weights ~N(0, 0.02)
+                w = (0.02 * torch.randn(n, k, device=dev, generator=g)).half()
+                mats[slot] = rt.make_mat(rt.FMT_F16, n, k, w)
+                keep.append(w)
+                continue
             u = torch.randint(1, 256, (n, k), dtype=torch.uint8, device=dev, generator=g)
             s = (torch.randn(k // GROUP, n, device=dev, generator=g).abs() * (0.02 / 127)).half()
             mats[slot] = rt.make_mat(rt.FMT_Q8, n, k, u, s, group=GROUP)
@@ -198,11 +209,15 @@ def time_q8_gemm(h, rt, torch, dev, M, iters=20):
     """Live roofline leg: the dominant kernel (mlp.layer1 q8 GEMM, M x 8192 x 2048, GELU epilogue)
     timed alone with CUDA events on the runtime's stream."""
     g = torch.Generator(device=dev).manual_seed(99)
-    u = torch.randint(1, 256, (F, D), dtype=torch.uint8, device=dev, generator=g)
-    s = (torch.randn(D // GROUP, F, device=dev, generator=g).abs() * (0.02 / 127)).half()
+    if FMT == "f16":
+        u = (0.02 * torch.randn(F, D, device=dev, generator=g)).half()
+        mat = rt.make_mat(rt.FMT_F16, F, D, u)
+    else:
+        u = torch.randint(1, 256, (F, D), dtype=torch.uint8, device=dev, generator=g)
+        s = (torch.randn(D // GROUP, F, device=dev, generator=g).abs() * (0.02 / 127)).half()
+        mat = rt.make_mat(rt.FMT_Q8, F, D, u, s, group=GROUP)
     A = torch.randn(M, D, device=dev, generator=g).half()
     out = torch.empty(M, F, dtype=torch.float16, device=dev)
-    mat = rt.make_mat(rt.FMT_Q8, F, D, u, s, group=GROUP)
     stream = torch.cuda.ExternalStream(h.stream())
     for _ in range(3):
         h.gemm(A, M, mat, rt.EPI_GELU, lda=D, out=out, ldo=F)
@@ -329,23 +344,26 @@ def run_ours(args, rank, world, local_rank):
             "metric": "images_per_sec", "value": value, "unit": "images/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "anima2.9b-q8-g64 512x768 4-step (config 3): 36 blocks x 4 steps, batch split over ranks",
+            "config": {"workload": (f"anima2b-f16 512x768 4-step (config 2): {NBLK} blocks x 4 steps, batch {images}"
+                                    if FMT == "f16" else
+                                    "anima2.9b-q8-g64 512x768 4-step (config 3): 36 blocks x 4 steps, batch split over ranks"),
                        "global_batch": images, "per_rank_batch": B, "tokens": T, "ctx_tokens": C, "hidden": D,
-                       "heads": HEADS, "ffn": F, "weights": "int8 g64 + fp16 scales", "blocks": NBLK, "steps": NSTEP,
+                       "heads": HEADS, "ffn": F, "weights": "fp16" if FMT == "f16" else "int8 g64 + fp16 scales",
+                       "blocks": NBLK, "steps": NSTEP,
                        "parallelism": f"dp{world} (image batch, no collective)",
-                       "l2": "weights 2.8 GB > L2: every step streams from HBM",
+                       "l2": f"weights {NBLK * (63 if FMT == 'q8' else 126) / 1000 + NBLK * 0.0126:.1f} GB > L2: every step streams from HBM",
                        "glue": "on GPU: timestep embedding, x_embedder, final layer, Euler (animad.cpp:423-492)",
                        "seed": 1234},
             "effective_tflops": flop_step / (ms * 1e-3) / 1e12,
             "roofline": {"bound": "tensor", "achieved": tf, "peak": peak_tf, "unit": "TFLOP/s", "frac": tf / peak_tf,
-                         "traffic": traffic, "kernel": f"q8 GEMM {B * T}x{F}x{D} GELU epilogue",
+                         "traffic": traffic if FMT == "q8" else None, "kernel": f"{FMT} GEMM {B * T}x{F}x{D} GELU epilogue",
                          "peak_kind": f"bf16 dense burst, {peak_kind}", "launch_ms": gms},
             "clocks": clk.summary(),
             "e2e": {"value": images / e2e_s, "unit": "images/s", "h2d_bytes_per_step": (latnbytes + cnbytes) * world,
                     "d2h_bytes_per_step": latnbytes * world},
             "gpu_launches": launches_per_sample,
             "cpu_baseline": {"value": cpu_img_s, "unit": "images/s", "cores": cores, "kind": "port",
-                             "sample": "oracle Anima block (torch fp32) at T=1536, 1 image, 1 block timed after 1 warm-up; images/s = 1/(t_block*36*4)"},
+                             "sample": f"oracle Anima block (torch fp32) at T=1536, 1 image, 1 block timed after 1 warm-up; images/s = 1/(t_block*{NBLK}*4)"},
         }
         print(json.dumps(line), flush=True)
     if dist:
@@ -372,8 +390,14 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=None, help="images over all ranks (config 3: 8, config 2: 1)")
+    ap.add_argument("--config", type=int, choices=[2, 3], default=3)
     args = ap.parse_args()
+    global NBLK, FMT
+    if args.config == 2:
+        NBLK, FMT = 28, "f16"
+    if args.batch is None:
+        args.batch = 1 if args.config == 2 else 8
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
