@@ -207,7 +207,8 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
       fence_proxy_async_smem();
       named_bar(1, EPI_WARPS * 32);
       if (threadIdx.x == 0) {
-        tma_store_2d(tmX, stage_ptr, n0 + 64 * g, m0);
+        if constexpr (EPI == EPI_GELU) tma_store_2d_evict_first(tmX, stage_ptr, n0 + 64 * g, m0);  // mlp hidden
+        else tma_store_2d(tmX, stage_ptr, n0 + 64 * g, m0);
         bulk_commit();
       }
     }

@@ -111,6 +111,17 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
       "r"(smem_u32(src)), "r"(x), "r"(y)
       : "memory");
 }
+// the same store with an L2 evict-first policy: for output streams far larger than L2 that would
+// otherwise push the GEMM's reused operand tiles out of L2
+__device__ __forceinline__ void tma_store_2d_evict_first(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile(
+      "{\n\t.reg .b64 pol;\n\t"
+      "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], pol;\n\t}" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(x), "r"(y)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // wait until at most N bulk groups still read their shared-memory sources
 template <int N>
