@@ -50,6 +50,7 @@ struct Cfg {
 struct KParams {
   int M, N, nkb, nkb1, group;
   int num_m_tiles, num_tiles;
+  int num_n_tiles, n_fastest;  // tile order: n_fastest walks the N tiles of one M block consecutively
   __half* out;
   int ldo;
   float* x;
@@ -65,6 +66,14 @@ struct KParams {
   float eps;
   int* status;
 };
+
+// tile t -> (M tile, N tile) in the launch's order
+__device__ __forceinline__ int tile_m(const KParams& p, int t) {
+  return p.n_fastest ? t / p.num_n_tiles : t % p.num_m_tiles;
+}
+__device__ __forceinline__ int tile_n(const KParams& p, int t) {
+  return p.n_fastest ? t % p.num_n_tiles : t / p.num_m_tiles;
+}
 
 // ---------------------------------------------------------------- dequantisers
 // One k-block (64 k) of a 256-row weight tile: raw smem -> fp16 SW128 K-major smem.
@@ -426,7 +435,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
         const int t = blockIdx.x + ti * gridDim.x;
-        const int m0 = (t % p.num_m_tiles) * BM, n0 = (t / p.num_m_tiles) * BN;
+        const int m0 = tile_m(p, t) * BM, n0 = tile_n(p, t) * BN;
         for (int kb = 0; kb < p.nkb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -505,7 +514,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     bool ok = true;
     for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
       const int t = blockIdx.x + ti * gridDim.x;
-      const int m0 = (t % p.num_m_tiles) * BM, n0 = (t / p.num_m_tiles) * BN;
+      const int m0 = tile_m(p, t) * BM, n0 = tile_n(p, t) * BN;
       const int acc = ti & 1;
       if (!mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 106)) { ok = false; break; }
       tc_fence_after();
@@ -629,7 +638,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
         const int t = pair + ti * npairs;
-        const int m0 = (t % p.num_m_tiles) * 2 * HALF + row0, n0 = (t / p.num_m_tiles) * BN + row0;
+        const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * BN + row0;
         for (int kb = 0; kb < p.nkb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -706,7 +715,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     bool ok = true;
     for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
       const int t = pair + ti * npairs;
-      const int m0 = (t % p.num_m_tiles) * 2 * HALF + row0, n0 = (t / p.num_m_tiles) * BN;
+      const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * BN;
       const int acc = ti & 1;
       if (!mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 116)) { ok = false; break; }
       tc_fence_after();
@@ -933,7 +942,16 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   p.nkb1 = a.K1 / BK;
   p.group = W->fmt == WF_F16 ? 64 : W->group;
   p.num_m_tiles = pair ? (a.M + 2 * HALF - 1) / (2 * HALF) : (a.M + BM - 1) / BM;
-  p.num_tiles = p.num_m_tiles * ((N + BN - 1) / BN);
+  p.num_n_tiles = (N + BN - 1) / BN;
+  p.num_tiles = p.num_m_tiles * p.num_n_tiles;
+  // default order walks M tiles under one weight block (the weight block stays in L2); when the A
+  // operand is far larger than L2 but the weights fit (the mlp down projection reading the 8-image
+  // hidden state), walk the N tiles of one A block instead so A streams from HBM once
+  {
+    const double a_bytes = static_cast<double>(a.M) * K * 2;
+    const double w_bytes = static_cast<double>(N) * K * (W->fmt == WF_F16 ? 2.0 : W->fmt == WF_Q8 ? 1.0 : 0.5);
+    p.n_fastest = a_bytes > 64e6 && w_bytes < 64e6 ? 1 : 0;
+  }
   p.out = a.out;
   p.ldo = a.ldo;
   p.x = a.x;

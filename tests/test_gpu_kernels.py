@@ -108,6 +108,22 @@ def test_gemm_residual(h, tile):
 
 
 @pytest.mark.parametrize("tile", TILES)
+def test_gemm_large_a_operand(h, tile):
+    """A larger than L2 (134 MB) with small weights: the launch walks the N tiles of each A block
+    consecutively; sampled rows against fp32 math."""
+    torch.manual_seed(41)
+    M, K, N = 8192, 8192, 512
+    Ad = (torch.randn(M, K, device="cuda") * 0.5).half()
+    mat, keep, Wd = make_mat(rt.FMT_Q8, (torch.randn(N, K) * 0.02).numpy(), 64)
+    out = torch.zeros(M, N, dtype=torch.float16, device="cuda")
+    h.gemm(Ad, M, mat, rt.EPI_STORE, lda=K, out=out, ldo=N, tile=tile)
+    h.sync()
+    rows = torch.cat((torch.arange(0, 256), torch.randint(256, M, (256,), generator=torch.Generator().manual_seed(42))))
+    ref = Ad[rows.cuda()].float().cpu() @ Wd.T
+    assert rel(out[rows.cuda()].float().cpu(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("tile", TILES)
 def test_gemm_rms_rope_segments(h, tile):
     torch.manual_seed(4)
     T, K, D = 192, 256, 256  # 2 heads per segment; q | k | v = 768 columns
