@@ -253,6 +253,92 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
       }
     }
   } else if constexpr (EPI == EPI_RMS) {
+    // Both 128-column heads of the tile in a RoPE segment (q or k): their rows share one token, so each
+    // chunk of 16 angles loads the row's cos / sin once for both heads.
+    auto segment = [&](int cb, const float*& g, int& rp) {
+      g = nullptr;
+      rp = 0;
+      if (cb < p.seg1) {
+        g = p.gain0;
+        rp = p.rope0;
+      } else if (cb < p.seg2) {
+        g = p.gain1;
+        rp = p.rope1;
+      }
+    };
+    const float *g0, *g1;
+    int rp0, rp1;
+    segment(n0, g0, rp0);
+    segment(n0 + 128, g1, rp1);
+    if (n0 + 128 < p.N && g0 && g1 && rp0 && rp1) {  // uniform over the epilogue warps
+      uint32_t r2[32];
+      float ss0 = 0.f, ss1 = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        tmem_ld32(tl + 32 * c, r);
+        tmem_ld32(tl + 128 + 32 * c, r2);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float t0 = __uint_as_float(r[i]), t1 = __uint_as_float(r2[i]);
+          ss0 = fmaf(t0, t0, ss0);
+          ss1 = fmaf(t1, t1, ss1);
+        }
+      }
+      const float rs0 = rsqrtf(ss0 * (1.0f / 128.0f) + p.eps), rs1 = rsqrtf(ss1 * (1.0f / 128.0f) + p.eps);
+      const int tok = row_ok ? m % p.rows_per_img : 0;
+      const float* cs = p.cosT + static_cast<size_t>(tok) * 64;
+      const float* sn = p.sinT + static_cast<size_t>(tok) * 64;
+      __half* orow = p.out + static_cast<size_t>(m) * p.ldo + n0;
+      uint32_t a16[16], b16[16];
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {  // 16 angles at a time: cos / sin loaded once, then each head's pairs
+        float cov[16], siv[16];
+        if (row_ok) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 co = *reinterpret_cast<const float4*>(cs + 16 * c + i);
+            const float4 si = *reinterpret_cast<const float4*>(sn + 16 * c + i);
+            cov[i] = co.x; cov[i + 1] = co.y; cov[i + 2] = co.z; cov[i + 3] = co.w;
+            siv[i] = si.x; siv[i + 1] = si.y; siv[i + 2] = si.z; siv[i + 3] = si.w;
+          }
+        }
+#pragma unroll 1
+        for (int hd = 0; hd < 2; ++hd) {
+          const float* g = hd ? g1 : g0;
+          const float rs = hd ? rs1 : rs0;
+          tmem_ld16(tl + 128 * hd + 16 * c, a16);
+          tmem_ld16(tl + 128 * hd + 64 + 16 * c, b16);
+          tmem_ld_wait();
+          if (!row_ok) continue;
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 ga = *reinterpret_cast<const float4*>(g + 16 * c + i);
+            const float4 gb = *reinterpret_cast<const float4*>(g + 16 * c + i + 64);
+            const float gav[4] = {ga.x, ga.y, ga.z, ga.w}, gbv[4] = {gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float av = __uint_as_float(a16[i + e]) * rs * gav[e];
+              const float bv = __uint_as_float(b16[i + e]) * rs * gbv[e];
+              a16[i + e] = __float_as_uint(av * cov[i + e] - bv * siv[i + e]);
+              b16[i + e] = __float_as_uint(bv * cov[i + e] + av * siv[i + e]);
+            }
+          }
+          uint4* lo4 = reinterpret_cast<uint4*>(orow + 128 * hd + 16 * c);
+          uint4* hi4 = reinterpret_cast<uint4*>(orow + 128 * hd + 64 + 16 * c);
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const float* fa = reinterpret_cast<const float*>(a16) + 8 * q;
+            const float* fb = reinterpret_cast<const float*>(b16) + 8 * q;
+            lo4[q] = make_uint4(pack_half2(fa[0], fa[1]), pack_half2(fa[2], fa[3]), pack_half2(fa[4], fa[5]),
+                                pack_half2(fa[6], fa[7]));
+            hi4[q] = make_uint4(pack_half2(fb[0], fb[1]), pack_half2(fb[2], fb[3]), pack_half2(fb[4], fb[5]),
+                                pack_half2(fb[6], fb[7]));
+          }
+        }
+      }
+      return;
+    }
 #pragma unroll 1
     for (int hh = 0; hh < BN / 128; ++hh) {
       const int cb = n0 + 128 * hh;
