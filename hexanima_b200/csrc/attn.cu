@@ -6,7 +6,8 @@
 // index >= nvalid get probability 0 (the reference masks the last key tile to -65504).
 // The reference folds 1/sqrt(128) into the q RMS gain (export_all.py:31-32), so scale = 1 there.
 //
-// One CTA per (256 queries = two 128-row Q tiles A and B, head, image). 10 warps:
+// Persistent: one CTA per SM walks items (256 queries = two 128-row Q tiles A and B, head, image), the
+// next item's Q, K and V loads overlapping the current item's softmax. 10 warps:
 //   warps 0-3  softmax of Q tile A, warps 4-7 softmax of Q tile B: thread = one query row (TMEM lane
 //              32(w%4) + lane); the two warps on an SMSP serve different Q tiles, so one's exps
 //              overlap the other's loads and the tensor core's work
@@ -56,6 +57,7 @@ __device__ __forceinline__ float ex2(float x) {
 
 struct AParams {
   int Tq, Tk, nvalid, H, nkt;
+  int B, nqp;  // images, 256-query blocks per image
   float scale_log2;
   __half* o;
   int ldo;
@@ -185,14 +187,28 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* p_full = bars + 11;   // [Q tile], one arrival per softmax warp of the tile
   uint64_t* pv_done = bars + 13;  // [Q tile], O_X += P_X V committed
   uint64_t* drain = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  uint64_t* q_empty = bars + 16;  // the item's S MMAs have read Q: the next item's Q may load
+  uint64_t* o_free = bars + 17;   // [Q tile], the softmax warps have read O_X: the next item may overwrite it
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qp = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int nkt = p.nkt;
+  // persistent: this CTA's items n = 0, 1, ... are blockIdx.x + n * gridDim.x; item -> (Q-tile pair, head,
+  // image) with the Q-tile pair fastest so that CTAs running at the same time share K and V in L2
+  const int nitems = p.nqp * p.H * p.B;
+  const int nmine = nitems > static_cast<int>(blockIdx.x)
+                        ? (nitems - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                        : 0;
+  auto item_of = [&](int n, int& qp, int& h, int& b) {
+    const int it = static_cast<int>(blockIdx.x) + n * static_cast<int>(gridDim.x);
+    qp = it % p.nqp;
+    h = (it / p.nqp) % p.H;
+    b = it / (p.nqp * p.H);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < KV_STAGES; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -203,6 +219,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       mbar_init(&s_full[x], 1);
       mbar_init(&p_full[x], 4);
       mbar_init(&pv_done[x], 1);
+      mbar_init(&o_free[x], 4);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -221,31 +238,39 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       prefetch_tmap(&tmQ);
       prefetch_tmap(&tmK);
       prefetch_tmap(&tmV);
-      const int qc = q_col0 + h * HD, kc = k_col0 + h * HD, vc = v_col0 + h * HD;
-      mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
-      for (int x = 0; x < 2; ++x) {
-        uint8_t* qb = smem + SMEM_Q + x * TILE_BYTES;
-        tma_load_3d(qb, &tmQ, q_full, qc, qp * QPAIR + x * QT, b);
-        tma_load_3d(qb + TILE_BYTES / 2, &tmQ, q_full, qc + 64, qp * QPAIR + x * QT, b);
+      int nq = 0, nk = 0, nv = 0;  // Q, K and V loads issued
+      bool ok = true;
+      for (int n = 0; n < nmine && ok; ++n) {
+        int qp, h, b;
+        item_of(n, qp, h, b);
+        const int qc = q_col0 + h * HD, kc = k_col0 + h * HD, vc = v_col0 + h * HD;
+        if (!mbar_wait(q_empty, (n & 1) ^ 1, p.status, 214)) { ok = false; break; }
+        mbar_arrive_expect_tx(q_full, 2 * TILE_BYTES);
+        for (int x = 0; x < 2; ++x) {
+          uint8_t* qb = smem + SMEM_Q + x * TILE_BYTES;
+          tma_load_3d(qb, &tmQ, q_full, qc, qp * QPAIR + x * QT, b);
+          tma_load_3d(qb + TILE_BYTES / 2, &tmQ, q_full, qc + 64, qp * QPAIR + x * QT, b);
+        }
+        ++nq;
+        for (int j = 0; j < nkt; ++j) {
+          const int g = n * nkt + j;
+          const int st = g & 1, ph = (g >> 1) & 1;
+          uint8_t* kb = smem + SMEM_K + st * TILE_BYTES;
+          uint8_t* vb = smem + SMEM_V + st * TILE_BYTES;
+          if (!mbar_wait(&k_empty[st], ph ^ 1, p.status, 201)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+          tma_load_3d(kb, &tmK, &k_full[st], kc, j * KT, b);
+          tma_load_3d(kb + TILE_BYTES / 2, &tmK, &k_full[st], kc + 64, j * KT, b);
+          ++nk;
+          if (!mbar_wait(&v_empty[st], ph ^ 1, p.status, 211)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+          tma_load_3d(vb, &tmV, &v_full[st], vc, j * KT, b);
+          tma_load_3d(vb + TILE_BYTES / 2, &tmV, &v_full[st], vc + 64, j * KT, b);
+          ++nv;
+        }
       }
-      int nk = 0, nv = 0;  // K and V tiles issued
-      for (int j = 0; j < nkt; ++j) {
-        const int st = j & 1, ph = (j >> 1) & 1;
-        uint8_t* kb = smem + SMEM_K + st * TILE_BYTES;
-        uint8_t* vb = smem + SMEM_V + st * TILE_BYTES;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, p.status, 201)) break;
-        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-        tma_load_3d(kb, &tmK, &k_full[st], kc, j * KT, b);
-        tma_load_3d(kb + TILE_BYTES / 2, &tmK, &k_full[st], kc + 64, j * KT, b);
-        ++nk;
-        if (!mbar_wait(&v_empty[st], ph ^ 1, p.status, 211)) break;
-        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-        tma_load_3d(vb, &tmV, &v_full[st], vc, j * KT, b);
-        tma_load_3d(vb + TILE_BYTES / 2, &tmV, &v_full[st], vc + 64, j * KT, b);
-        ++nv;
-      }
-      if (nv < nkt) {  // aborted: let the copies in flight land before the CTA exits
-        mbar_wait(q_full, 0, nullptr, 0);
+      if (!ok) {  // aborted: let the copies in flight land before the CTA exits
+        if (nq > 0) mbar_wait(q_full, (nq - 1) & 1, nullptr, 0);
         for (int i = (nk > KV_STAGES ? nk - KV_STAGES : 0); i < nk; ++i)
           mbar_wait(&k_full[i & 1], (i >> 1) & 1, nullptr, 0);
         for (int i = (nv > KV_STAGES ? nv - KV_STAGES : 0); i < nv; ++i)
@@ -256,13 +281,14 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16(QT, KT, 0, 0);  // S = Q K^T, both K-major
       constexpr uint32_t id_o = idesc_f16(QT, HD, 0, 1);  // O += P V, P K-major in TMEM, V MN-major
-      bool ok = mbar_wait(q_full, 0, p.status, 202);
+      bool ok = true;
       bool issued = false;
-      auto issue_s = [&](int x, int j) -> bool {  // S_x(j); P_x(j-1) must have been read by O_x += P V
-        if (j > 0 && !mbar_wait(&pv_done[x], (j - 1) & 1, p.status, 203)) return false;
+      // S_x(g): P_x(g-1) (aliasing S_x) must have been read by O_x += P V
+      auto issue_s = [&](int x, int g) -> bool {
+        if (g > 0 && !mbar_wait(&pv_done[x], (g - 1) & 1, p.status, 203)) return false;
         tc_fence_after();
         const uint32_t q0 = smem_u32(smem + SMEM_Q + x * TILE_BYTES);
-        const uint32_t kb = smem_u32(smem + SMEM_K + (j & 1) * TILE_BYTES);
+        const uint32_t kb = smem_u32(smem + SMEM_K + (g & 1) * TILE_BYTES);
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint32_t off = (k >> 2) * (TILE_BYTES / 2) + 32 * (k & 3);
@@ -273,38 +299,47 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         mma_commit(&s_full[x]);
         return true;
       };
-      auto issue_pv = [&](int x, int j) -> bool {
-        if (!mbar_wait(&p_full[x], j & 1, p.status, 204)) return false;
+      // O_x (+)= P_x(g) V(g); the first tile of an item overwrites O_x once the previous item's O_x was read
+      auto issue_pv = [&](int x, int g, int n, bool first) -> bool {
+        if (!mbar_wait(&p_full[x], g & 1, p.status, 204)) return false;
+        if (first && n > 0 && !mbar_wait(&o_free[x], (n - 1) & 1, p.status, 215)) return false;
         tc_fence_after();
-        const uint32_t vb = smem_u32(smem + SMEM_V + (j & 1) * TILE_BYTES);
+        const uint32_t vb = smem_u32(smem + SMEM_V + (g & 1) * TILE_BYTES);
 #pragma unroll
         for (int k = 0; k < KT / 16; ++k) {
           const uint64_t bd = sdesc_sw128(vb + 2048 * k, TILE_BYTES / 2, 1024);
-          mma_f16_ts(tmem + TM_O + x * 128, tmem + TM_S + x * 128 + 8 * k, bd, id_o, (j > 0 || k != 0) ? 1u : 0u);
+          mma_f16_ts(tmem + TM_O + x * 128, tmem + TM_S + x * 128 + 8 * k, bd, id_o, (!first || k != 0) ? 1u : 0u);
         }
         issued = true;
         mma_commit(&pv_done[x]);
         return true;
       };
-      // S_A(0) S_B(0), then per tile j: PV_A(j) S_A(j+1) PV_B(j) S_B(j+1)
-      if (ok && nkt > 0) {
-        ok = mbar_wait(&k_full[0], 0, p.status, 205) && issue_s(0, 0) && issue_s(1, 0);
-        if (ok) mma_commit(&k_empty[0]);
-      }
-      for (int j = 0; j < nkt && ok; ++j) {
-        const bool more = j + 1 < nkt;
-        const int st1 = (j + 1) & 1;
-        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, p.status, 206)) { ok = false; break; }
-        if (!issue_pv(0, j)) { ok = false; break; }
-        if (more && !(mbar_wait(&k_full[st1], ((j + 1) >> 1) & 1, p.status, 207) && issue_s(0, j + 1))) {
+      for (int n = 0; n < nmine && ok; ++n) {
+        const int g0 = n * nkt;
+        // per tile: PV_A(g) S_A(g+1) PV_B(g) S_B(g+1); the item starts with S_A(g0) S_B(g0)
+        if (!(mbar_wait(q_full, n & 1, p.status, 202) && mbar_wait(&k_full[g0 & 1], (g0 >> 1) & 1, p.status, 205) &&
+              issue_s(0, g0) && issue_s(1, g0))) {
           ok = false;
           break;
         }
-        if (!issue_pv(1, j)) { ok = false; break; }
-        mma_commit(&v_empty[j & 1]);
-        if (more) {
-          if (!issue_s(1, j + 1)) { ok = false; break; }
-          mma_commit(&k_empty[st1]);
+        mma_commit(&k_empty[g0 & 1]);
+        if (nkt == 1) mma_commit(q_empty);
+        for (int j = 0; j < nkt && ok; ++j) {
+          const int g = g0 + j;
+          const bool more = j + 1 < nkt;
+          if (!mbar_wait(&v_full[g & 1], (g >> 1) & 1, p.status, 206)) { ok = false; break; }
+          if (!issue_pv(0, g, n, j == 0)) { ok = false; break; }
+          if (more && !(mbar_wait(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, p.status, 207) && issue_s(0, g + 1))) {
+            ok = false;
+            break;
+          }
+          if (!issue_pv(1, g, n, j == 0)) { ok = false; break; }
+          mma_commit(&v_empty[g & 1]);
+          if (more) {
+            if (!issue_s(1, g + 1)) { ok = false; break; }
+            mma_commit(&k_empty[(g + 1) & 1]);
+            if (j + 2 == nkt) mma_commit(q_empty);  // the item's last S is issued: Q may be replaced
+          }
         }
       }
       if (!ok && issued) {
@@ -313,125 +348,129 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       }
     }
   } else {
-    // softmax warps: thread owns query row `row` of Q tile `qx`
-    const int qx = warp >> 2, g = warp & 3;
-    const int row = g * 32 + lane;
-    const uint32_t tl = static_cast<uint32_t>(g * 32) << 16;
+    // softmax warps: thread owns query row `row` of Q tile `qx` of each item
+    const int qx = warp >> 2, g4 = warp & 3;
+    const int row = g4 * 32 + lane;
+    const uint32_t tl = static_cast<uint32_t>(g4 * 32) << 16;
     const uint32_t tS = tmem + tl + TM_S + qx * 128, tO = tmem + tl + TM_O + qx * 128;
     const int limit = p.nvalid;  // keys >= limit are masked
     const uint64_t scale2 = f2pack(p.scale_log2, p.scale_log2);
-    float m_ref = 0.f, l_run = 0.f;
     uint32_t sa[32], r[32];
     bool ok = true;
-    for (int j = 0; j < nkt && ok; ++j) {
-      if (!warp_wait(&s_full[qx], j & 1, p.status, 208)) { ok = false; break; }
-      tc_fence_after();
-      const int key0 = j * KT;
-      const bool full_tile = key0 + KT <= limit;
-      // row max: keys 64..127 first, then keys 0..63 stay in registers for the exp pass
-      float mxp[8];
+    for (int n = 0; n < nmine && ok; ++n) {
+      int qp, h, b;
+      item_of(n, qp, h, b);
+      float m_ref = 0.f, l_run = 0.f;
+      for (int j = 0; j < nkt && ok; ++j) {
+        const int g = n * nkt + j;
+        if (!warp_wait(&s_full[qx], g & 1, p.status, 208)) { ok = false; break; }
+        tc_fence_after();
+        const int key0 = j * KT;
+        const bool full_tile = key0 + KT <= limit;
+        // row max: keys 64..127 first, then keys 0..63 stay in registers for the exp pass
+        float mxp[8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) mxp[t] = -INFINITY;
-      tmem_ld32(tS + 64, sa);
-      tmem_ld32(tS + 96, r);
-      tmem_ld_wait();
-      if (full_tile) {
-        max32<true>(mxp, sa, key0 + 64, limit);
-        max32<true>(mxp, r, key0 + 96, limit);
-      } else {
-        max32<false>(mxp, sa, key0 + 64, limit);
-        max32<false>(mxp, r, key0 + 96, limit);
-      }
-      tmem_ld32(tS, sa);
-      tmem_ld32(tS + 32, r);
-      tmem_ld_wait();
-      if (full_tile) {
-        max32<true>(mxp, sa, key0, limit);
-        max32<true>(mxp, r, key0 + 32, limit);
-      } else {
-        max32<false>(mxp, sa, key0, limit);
-        max32<false>(mxp, r, key0 + 32, limit);
-      }
-      const float mt =
-          fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])) * p.scale_log2;
-      if (j == 0) {
-        m_ref = mt == -INFINITY ? 0.f : mt;  // O_X is written fresh by the first P V
-      } else {
-        const bool need = mt > m_ref + RESCALE_LOG2;
-        if (__any_sync(0xffffffffu, need)) {
-          // O_X += P_X(j-1) V has completed (S_X(j) was issued after it); P_X(j) is not published yet
-          const float alpha = need ? ex2(m_ref - mt) : 1.f;
-          if (need) m_ref = mt;
-          l_run *= alpha;
-          const uint64_t a2 = f2pack(alpha, alpha);
-          uint32_t ob[32];
-#pragma unroll
-          for (int c = 0; c < HD / 32; ++c) {
-            tmem_ld32(tO + 32 * c, ob);
-            tmem_ld_wait();
-            uint32_t w0[16], w1[16];
-#pragma unroll
-            for (int t = 0; t < 8; ++t) {
-              float x0, x1;
-              f2unpack(ffma2(f2pack(__uint_as_float(ob[2 * t]), __uint_as_float(ob[2 * t + 1])), a2, 0ull), x0, x1);
-              w0[2 * t] = __float_as_uint(x0);
-              w0[2 * t + 1] = __float_as_uint(x1);
-              f2unpack(ffma2(f2pack(__uint_as_float(ob[16 + 2 * t]), __uint_as_float(ob[17 + 2 * t])), a2, 0ull), x0,
-                       x1);
-              w1[2 * t] = __float_as_uint(x0);
-              w1[2 * t + 1] = __float_as_uint(x1);
-            }
-            tmem_st16(tO + 32 * c, w0);
-            tmem_st16(tO + 32 * c + 16, w1);
-          }
-        }
-      }
-      const uint64_t negm2 = f2pack(-m_ref, -m_ref);
-      uint64_t sum2[4] = {0, 0, 0, 0};
-      {
-        // keys 0..63 (registers) -> P columns 0..31, then keys 64..127 -> P columns 32..63; each P column
-        // overwrites S columns this thread has already read
-        uint32_t pk[16];
-        if (full_tile) {
-          exp32<true>(pk, sum2, sa, scale2, negm2, key0, limit);
-          tmem_st16(tS, pk);
-          exp32<true>(pk, sum2, r, scale2, negm2, key0 + 32, limit);
-          tmem_st16(tS + 16, pk);
-        } else {
-          exp32<false>(pk, sum2, sa, scale2, negm2, key0, limit);
-          tmem_st16(tS, pk);
-          exp32<false>(pk, sum2, r, scale2, negm2, key0 + 32, limit);
-          tmem_st16(tS + 16, pk);
-        }
+        for (int t = 0; t < 8; ++t) mxp[t] = -INFINITY;
         tmem_ld32(tS + 64, sa);
         tmem_ld32(tS + 96, r);
         tmem_ld_wait();
         if (full_tile) {
-          exp32<true>(pk, sum2, sa, scale2, negm2, key0 + 64, limit);
-          tmem_st16(tS + 32, pk);
-          exp32<true>(pk, sum2, r, scale2, negm2, key0 + 96, limit);
-          tmem_st16(tS + 48, pk);
+          max32<true>(mxp, sa, key0 + 64, limit);
+          max32<true>(mxp, r, key0 + 96, limit);
         } else {
-          exp32<false>(pk, sum2, sa, scale2, negm2, key0 + 64, limit);
-          tmem_st16(tS + 32, pk);
-          exp32<false>(pk, sum2, r, scale2, negm2, key0 + 96, limit);
-          tmem_st16(tS + 48, pk);
+          max32<false>(mxp, sa, key0 + 64, limit);
+          max32<false>(mxp, r, key0 + 96, limit);
         }
+        tmem_ld32(tS, sa);
+        tmem_ld32(tS + 32, r);
+        tmem_ld_wait();
+        if (full_tile) {
+          max32<true>(mxp, sa, key0, limit);
+          max32<true>(mxp, r, key0 + 32, limit);
+        } else {
+          max32<false>(mxp, sa, key0, limit);
+          max32<false>(mxp, r, key0 + 32, limit);
+        }
+        const float mt =
+            fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])) * p.scale_log2;
+        if (j == 0) {
+          m_ref = mt == -INFINITY ? 0.f : mt;  // O_X is written fresh by the item's first P V
+        } else {
+          const bool need = mt > m_ref + RESCALE_LOG2;
+          if (__any_sync(0xffffffffu, need)) {
+            // O_X += P_X(g-1) V has completed (S_X(g) was issued after it); P_X(g) is not published yet
+            const float alpha = need ? ex2(m_ref - mt) : 1.f;
+            if (need) m_ref = mt;
+            l_run *= alpha;
+            const uint64_t a2 = f2pack(alpha, alpha);
+            uint32_t ob[32];
+#pragma unroll
+            for (int c = 0; c < HD / 32; ++c) {
+              tmem_ld32(tO + 32 * c, ob);
+              tmem_ld_wait();
+              uint32_t w0[16], w1[16];
+#pragma unroll
+              for (int t = 0; t < 8; ++t) {
+                float x0, x1;
+                f2unpack(ffma2(f2pack(__uint_as_float(ob[2 * t]), __uint_as_float(ob[2 * t + 1])), a2, 0ull), x0, x1);
+                w0[2 * t] = __float_as_uint(x0);
+                w0[2 * t + 1] = __float_as_uint(x1);
+                f2unpack(ffma2(f2pack(__uint_as_float(ob[16 + 2 * t]), __uint_as_float(ob[17 + 2 * t])), a2, 0ull),
+                         x0, x1);
+                w1[2 * t] = __float_as_uint(x0);
+                w1[2 * t + 1] = __float_as_uint(x1);
+              }
+              tmem_st16(tO + 32 * c, w0);
+              tmem_st16(tO + 32 * c + 16, w1);
+            }
+          }
+        }
+        const uint64_t negm2 = f2pack(-m_ref, -m_ref);
+        uint64_t sum2[4] = {0, 0, 0, 0};
+        {
+          // keys 0..63 (registers) -> P columns 0..31, then keys 64..127 -> P columns 32..63; each P column
+          // overwrites S columns this thread has already read
+          uint32_t pk[16];
+          if (full_tile) {
+            exp32<true>(pk, sum2, sa, scale2, negm2, key0, limit);
+            tmem_st16(tS, pk);
+            exp32<true>(pk, sum2, r, scale2, negm2, key0 + 32, limit);
+            tmem_st16(tS + 16, pk);
+          } else {
+            exp32<false>(pk, sum2, sa, scale2, negm2, key0, limit);
+            tmem_st16(tS, pk);
+            exp32<false>(pk, sum2, r, scale2, negm2, key0 + 32, limit);
+            tmem_st16(tS + 16, pk);
+          }
+          tmem_ld32(tS + 64, sa);
+          tmem_ld32(tS + 96, r);
+          tmem_ld_wait();
+          if (full_tile) {
+            exp32<true>(pk, sum2, sa, scale2, negm2, key0 + 64, limit);
+            tmem_st16(tS + 32, pk);
+            exp32<true>(pk, sum2, r, scale2, negm2, key0 + 96, limit);
+            tmem_st16(tS + 48, pk);
+          } else {
+            exp32<false>(pk, sum2, sa, scale2, negm2, key0 + 64, limit);
+            tmem_st16(tS + 32, pk);
+            exp32<false>(pk, sum2, r, scale2, negm2, key0 + 96, limit);
+            tmem_st16(tS + 48, pk);
+          }
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[qx]);
+        const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
+        float slo, shi;
+        f2unpack(s01, slo, shi);
+        l_run += slo + shi;
       }
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[qx]);
-      const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
-      float slo, shi;
-      f2unpack(s01, slo, shi);
-      l_run += slo + shi;
-    }
-    // the last O_X += P_X V: earlier ones completed before S_X(nkt-1) was issued
-    if (ok && nkt > 0) ok = warp_wait(&pv_done[qx], (nkt - 1) & 1, p.status, 209);
-    const int q = qp * QPAIR + qx * QT + row;
-    if (ok) {  // warp-uniform: every lane takes part in the TMEM loads, rows past Tq store nothing
+      if (!ok) break;
+      // the item's last O_X += P_X V: earlier ones completed before its last S_X was issued
+      if (!warp_wait(&pv_done[qx], (n * nkt + nkt - 1) & 1, p.status, 209)) { ok = false; break; }
       tc_fence_after();
+      const int q = qp * QPAIR + qx * QT + row;
       const bool live = q < p.Tq;
       const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
       uint4* d4 = reinterpret_cast<uint4*>(p.o + (static_cast<size_t>(b) * p.Tq + (live ? q : 0)) * p.ldo + h * HD);
@@ -439,6 +478,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       for (int c = 0; c < HD / 32; ++c) {
         tmem_ld32(tO + 32 * c, sa);
         tmem_ld_wait();
+        if (c == HD / 32 - 1) {  // all of O_X read: the next item's first P V may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_free[qx]);
+        }
         if (live) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -494,7 +538,10 @@ cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s) {
   p.o = a.o;
   p.ldo = a.ldo;
   p.status = a.status;
-  dim3 grid((a.Tq + QPAIR - 1) / QPAIR, a.H, a.B);
+  p.B = a.B;
+  p.nqp = (a.Tq + QPAIR - 1) / QPAIR;
+  const long nitems = static_cast<long>(p.nqp) * a.H * a.B;
+  const int grid = static_cast<int>(nitems < sm_count() ? nitems : sm_count());
   attn_kernel<<<grid, ATT_THREADS, ATT_SMEM, s>>>(tQ, tK, tV, p, a.q_col0, a.k_col0, a.v_col0);
   return cudaGetLastError();
 }
