@@ -974,6 +974,13 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   if (W->fmt == WF_Q8 && W->group != 32 && W->group != 64) return cudaErrorInvalidValue;
   if ((W->fmt == WF_Q4 || W->fmt == WF_Q4A) && W->group != 32) return cudaErrorInvalidValue;
 
+  // q8 weights: the kernel that keeps the dequantised weights in TMEM takes the RMS (q/k/v projection)
+  // epilogue when its tiles fill the GPU; measured on the 8-image block shapes it is 2-3 % faster there
+  // and 3-7 % slower than the CTA-pair kernel with the store, GELU and residual epilogues
+  if (a.tile == 3) return gemm_wt_launch(a, s);
+  if (a.tile == 0 && a.epi == EPI_RMS && gemm_wt_eligible(a) && gemm_wt_tiles(a) >= sm_count() / 2)
+    return gemm_wt_launch(a, s);
+
   // tile configuration: CTA pairs (256x256 per cluster) when there are enough pair tiles to fill the
   // GPU (M1 shape, 8 images: q8 1098 vs 869 TFLOP/s, fp16 1230 vs 1160), else single-CTA 128x256
   // tiles (small M: the context GEMM, one image)

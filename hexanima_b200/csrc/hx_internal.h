@@ -58,7 +58,7 @@ struct GemmArgs {
   float eps = 1e-6f;
   int* status = nullptr;
   int max_ctas = 0;  // 0 = one CTA per SM
-  int tile = 0;      // 0 auto, 1 single-CTA 128x256 tiles, 2 CTA-pair 256x256 tiles
+  int tile = 0;      // 0 auto, 1 single-CTA 128x256 tiles, 2 CTA-pair 256x256 tiles, 3 weights in TMEM
 };
 
 struct AttnArgs {
@@ -78,6 +78,12 @@ struct AttnArgs {
 };
 
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s);
+// q8 GEMM with the dequantised weights in TMEM (gemm_wt.cu): STORE / GELU / RESID / RMS epilogues,
+// N a multiple of 256; gemm_launch picks it for the RMS epilogue when its tiles fill the GPU (tile 3
+// forces it)
+bool gemm_wt_eligible(const GemmArgs& a);
+int gemm_wt_tiles(const GemmArgs& a);
+cudaError_t gemm_wt_launch(const GemmArgs& a, cudaStream_t s);
 cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s);
 
 // memory-bound kernels (elem.cu)

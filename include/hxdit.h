@@ -318,7 +318,7 @@ typedef struct {
   int seg1, seg2, rope0, rope1;
   const float* cos_t; const float* sin_t;   /* [rows_per_img][64] */
   float eps;
-  int tile;                     /* 0 auto, 1 single-CTA 128x256 tiles, 2 CTA-pair 256x256 tiles */
+  int tile;                     /* 0 auto, 1 single-CTA 128x256, 2 CTA-pair 256x256, 3 q8 weights in TMEM */
 } hx_gemm_desc;
 #define HX_EPI_STORE 0
 #define HX_EPI_RESID 1

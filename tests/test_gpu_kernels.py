@@ -25,6 +25,7 @@ def h():
 
 
 TILES = [1, 2]  # single-CTA 128x256 tiles, CTA-pair 256x256 tiles (cta_group::2)
+TILES3 = [1, 2, 3]  # + q8 weights dequantised into TMEM (256 weight rows x 192 tokens per CTA pair)
 
 
 def _onehot_dequant(h, fmt, w, group, tile):
@@ -38,12 +39,14 @@ def _onehot_dequant(h, fmt, w, group, tile):
     return out.cpu().T.contiguous(), deq
 
 
-@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("tile", TILES3)
 @pytest.mark.parametrize("fmt,group", [(rt.FMT_F16, 64), (rt.FMT_Q8, 32), (rt.FMT_Q8, 64), (rt.FMT_Q4, 32),
                                        (rt.FMT_Q4A, 32)])
 def test_dequant_bit_exact(h, fmt, group, tile):
+    if tile == 3 and fmt != rt.FMT_Q8:
+        pytest.skip("the TMEM-weight kernel takes q8 weights")
     rng = np.random.default_rng(7)
-    N, K = 320, 256
+    N, K = (512 if tile == 3 else 320), 256
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
     w[3] *= 1e-3     # small scales: subnormal fp16 products
     w[7] *= 300.0    # large values
@@ -57,11 +60,13 @@ def _ref_gemm(A16, Wd):
     return A16.float().cpu() @ Wd.T
 
 
-@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("tile", TILES3)
 @pytest.mark.parametrize("fmt", [rt.FMT_F16, rt.FMT_Q8, rt.FMT_Q4])
 def test_gemm_store_and_gelu(h, fmt, tile):
+    if tile == 3 and fmt != rt.FMT_Q8:
+        pytest.skip("the TMEM-weight kernel takes q8 weights")
     torch.manual_seed(1)
-    M, K, N = 300, 512, 544
+    M, K, N = 300, 512, (512 if tile == 3 else 544)
     A = torch.randn(M, K).half()
     mat, keep, Wd = make_mat(fmt, (torch.randn(N, K) * 0.05).numpy(), 32)
     ref = _ref_gemm(A, Wd)
@@ -72,7 +77,7 @@ def test_gemm_store_and_gelu(h, fmt, tile):
         assert rel(out.float(), f(ref)) < 2e-3
 
 
-@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("tile", TILES3)
 def test_gemm_large_k_and_lora_a2(h, tile):
     torch.manual_seed(2)
     M, K1, N = 256, 8192, 512
@@ -90,7 +95,7 @@ def test_gemm_large_k_and_lora_a2(h, tile):
     assert rel(out.float(), ref) < 2e-3
 
 
-@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("tile", TILES3)
 def test_gemm_residual(h, tile):
     torch.manual_seed(3)
     B, T, K, N = 2, 160, 256, 512
@@ -107,7 +112,7 @@ def test_gemm_residual(h, tile):
     assert rel(x.cpu() - x0, ref - x0) < 2e-3
 
 
-@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("tile", TILES3)
 def test_gemm_large_a_operand(h, tile):
     """A larger than L2 (134 MB) with small weights: the launch walks the N tiles of each A block
     consecutively; sampled rows against fp32 math."""
@@ -123,12 +128,13 @@ def test_gemm_large_a_operand(h, tile):
     assert rel(out[rows.cuda()].float().cpu(), ref) < 2e-3
 
 
-@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("tile", TILES3)
 def test_gemm_rms_rope_segments(h, tile):
     torch.manual_seed(4)
     T, K, D = 192, 256, 256  # 2 heads per segment; q | k | v = 768 columns
     A = torch.randn(T, K).half()
-    mat, keep, Wd = make_mat(rt.FMT_F16, (torch.randn(3 * D, K) * 0.05).numpy())
+    fmt = rt.FMT_Q8 if tile == 3 else rt.FMT_F16
+    mat, keep, Wd = make_mat(fmt, (torch.randn(3 * D, K) * 0.05).numpy(), 64)
     gq, gk = 1 + 0.1 * torch.randn(128), 1 + 0.1 * torch.randn(128)
     ang = torch.rand(T, 64) * 6.0
     cos, sin = torch.cos(ang), torch.sin(ang)
