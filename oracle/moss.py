@@ -131,10 +131,14 @@ def block_dev(x, mod, cos64, sin64, mats, gain, nvalid=None, lora=True, heads=No
     q = rot(rms(q.view(B, T, H, HD), qg))
     k = rot(rms(k.view(B, T, H, HD), kg))
     v = v.view(B, T, H, HD)
-    sc = torch.einsum("bqhd,bkhd->bhqk", q, k)
-    if nvalid is not None and nvalid < T:
-        sc[..., nvalid:] = float("-inf")
-    a = torch.einsum("bhqk,bkhd->bqhd", torch.softmax(sc, -1), v).reshape(B, T, D)
+    # attention in groups of heads (the same per-head math; bounds host memory at the large configs)
+    a = torch.empty(B, T, H, HD, dtype=q.dtype)
+    for h0 in range(0, H, 4):
+        sc = torch.einsum("bqhd,bkhd->bhqk", q[:, :, h0:h0 + 4], k[:, :, h0:h0 + 4])
+        if nvalid is not None and nvalid < T:
+            sc[..., nvalid:] = float("-inf")
+        a[:, :, h0:h0 + 4] = torch.einsum("bhqk,bkhd->bqhd", torch.softmax(sc, -1), v[:, :, h0:h0 + 4])
+    a = a.reshape(B, T, D)
     o = (cat(a, LA(a, "ao")) if lora else a) @ mats["o"].T
     x = x + o * ga
     y2 = rms(x, n2) * (1 + cf) + sf
