@@ -1018,6 +1018,28 @@ int hx_lora_fold(hx_handle hh, int wfd, int slot, const float* B, const float* A
   return e == cudaSuccess ? HX_OK : e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA;
 }
 
+int hx_lora_fold_slots(hx_handle hh, int wfd, int proj, const float* B, const float* A, int rank, float scale) {
+  hx_ctx* h = H(hh);
+  if (!h || !B || !A || proj < HX_LORA_Q || proj > HX_LORA_DN || rank < 1 || rank > 128) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto it = h->weights.find(wfd);
+  if (it == h->weights.end()) return HX_E_NOWEIGHTS;
+  const Weights& W = *it->second;
+  if (W.model != HX_MODEL_MOSS || !W.lora) return HX_E_FORMAT;
+  static const int kSlot[6] = {HX_W_Q, HX_W_K, HX_W_V, HX_W_O, HX_W_M1, HX_W_M2};
+  static const int kA[6] = {HX_W_AQKV, HX_W_AQKV, HX_W_AQKV, HX_W_AO, HX_W_AUG, HX_W_ADN};
+  static const int kRow0[6] = {0, 128, 256, 0, 0, 0};
+  const int slot = kSlot[proj], aslot = kA[proj];
+  if (!W.has[slot] || !W.has[aslot]) return HX_E_ARG;
+  const DevMat& M = W.mats[slot];
+  const DevMat& Am = W.mats[aslot];
+  if (M.fmt != HX_FMT_Q8 || Am.fmt != HX_FMT_Q8) return HX_E_FORMAT;
+  DevGuard g(h->device);
+  const cudaError_t e = lora_fold_slots(M, M.K - 128, proj == HX_LORA_UG ? 1 : 0, Am, kRow0[proj], B, A, rank, scale,
+                                        h->stream);
+  return e == cudaSuccess ? HX_OK : e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA;
+}
+
 int hx_pack_apply_overlay(void* pack, size_t pack_bytes, const void* ovl, size_t ovl_bytes) {
   if (!pack || !ovl || ovl_bytes < 4) return HX_E_ARG;
   const uint8_t* o = static_cast<const uint8_t*>(ovl);

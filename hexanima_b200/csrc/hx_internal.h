@@ -121,6 +121,10 @@ cudaError_t repack_tiles_launch(const uint8_t* rec, int nb, int kb, bool q8, voi
 // (lora.cu). row_mode 1: MOSS up_gate device row order; floor_mode 0 MOSS, 1 Anima scale floor.
 cudaError_t lora_fold_launch(const DevMat& W, int k_base, const float* B, const float* A, int rank, float lscale,
                              int row_mode, int floor_mode, cudaStream_t s);
+// the rank-128 LoRA slot fold (lorasvd.cu): W the LoRA-carrying matrix (K = k_base + 128), A the
+// LoRA-A matrix whose rows a_row0 .. +127 are the slots; synchronous on s
+cudaError_t lora_fold_slots(const DevMat& W, int k_base, int row_mode, const DevMat& A, int a_row0, const float* Bu,
+                            const float* Au, int rank, float scale, cudaStream_t s);
 int sm_count();
 
 }  // namespace hx

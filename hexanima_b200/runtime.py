@@ -25,6 +25,7 @@ ERRORS = {-1: "HX_E_ARG", -2: "HX_E_CUDA", -5: "HX_E_NOWEIGHTS", -6: "HX_E_NOBLO
 
 MODEL_ANIMA, MODEL_MOSS, MODEL_MOSS_PROJ = 1, 2, 3
 FMT_F16, FMT_Q8, FMT_Q4A, FMT_Q4 = 0, 1, 2, 3
+LORA_Q, LORA_K, LORA_V, LORA_O, LORA_UG, LORA_DN = 0, 1, 2, 3, 4, 5  # projections with rank-128 LoRA slots
 EPI_STORE, EPI_RESID, EPI_GELU, EPI_RMS, EPI_SITU, EPI_STORE32 = 0, 1, 2, 3, 5, 6
 (W_QKV, W_O, W_CQ, W_CKV, W_CO, W_M1, W_M2, W_Q, W_K, W_V, W_AQKV, W_AO, W_AUG, W_ADN) = range(14)
 NMATS = 14
@@ -123,6 +124,7 @@ _SIGS = {
     "hx_weights_bind": [_vp, ctypes.POINTER(hx_weight_desc), ctypes.POINTER(_i)],
     "hx_weights_free": [_vp, _i],
     "hx_lora_fold": [_vp, _i, _i, _vp, _vp, _i, _f],
+    "hx_lora_fold_slots": [_vp, _i, _i, _vp, _vp, _i, _f],
     "hx_pack_apply_overlay": [_vp, _sz, _vp, _sz],
     "hx_blob_layout": [_i, _i, _i, _i, _i, _i, _i, _ip, _i, ctypes.POINTER(_sz)],
     "hx_mega_block": [_vp, _ip, _i, _i, _i, _vp, _i, _ip, _i, _ip],
@@ -325,6 +327,12 @@ class Handle:
     def lora_fold(self, wfd, slot, B_dev, A_dev, rank, scale=1.0):
         """Fold scale * B[N][rank] @ A[rank][K_base] (device fp32) into the q8 matrix `slot` of wfd, in place."""
         _check(lib().hx_lora_fold(self.h, wfd, slot, _ptr(B_dev), _ptr(A_dev), rank, scale), "hx_lora_fold")
+
+    def lora_fold_slots(self, wfd, proj, B_dev, A_dev, rank, scale=1.0):
+        """Fold scale * B[N][rank] @ A[rank][K_base] (device fp32, B in logical row order) into the rank-128
+        LoRA slots of MOSS projection `proj` (LORA_Q .. LORA_DN): best rank-128 approximation, requantised."""
+        _check(lib().hx_lora_fold_slots(self.h, wfd, proj, _ptr(B_dev), _ptr(A_dev), rank, scale),
+               "hx_lora_fold_slots")
 
     # -------------------------------------------------------------- block / chain
     def mega_block(self, meta, wfd, bfd, mod=None, ntimes=0):

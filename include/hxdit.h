@@ -139,6 +139,25 @@ HX_API int hx_weights_free(hx_handle h, int wfd);
  * (caller-owned) weights are modified too. Runs on the handle's stream. */
 HX_API int hx_lora_fold(hx_handle h, int wfd, int slot, const float* B_dev, const float* A_dev, int rank, float scale);
 
+/* Projections of a MOSS block that carry rank-128 LoRA slots (export_moss.py:14-27). */
+#define HX_LORA_Q 0   /* slots: HX_W_Q K columns [D, D+128) and HX_W_AQKV rows [0, 128) */
+#define HX_LORA_K 1   /* HX_W_K, HX_W_AQKV rows [128, 256) */
+#define HX_LORA_V 2   /* HX_W_V, HX_W_AQKV rows [256, 384) */
+#define HX_LORA_O 3   /* HX_W_O, HX_W_AO */
+#define HX_LORA_UG 4  /* HX_W_M1 (up_gate), HX_W_AUG */
+#define HX_LORA_DN 5  /* HX_W_M2 (ffn_down), HX_W_ADN */
+/* Fold scale * B * A into the rank-128 LoRA slots of projection `proj` of a MOSS q8 weight set with
+ * LoRA (desc.lora = 1 or a MOSS pack): the slots become the best rank-128 approximation of their
+ * current delta plus scale * B * A, found by the Gram-eigen / SVD route of the reference's fold tool
+ * (moss/mossrun/lorafold.cpp:200-284 `fold`, singular values on the B side), and are requantised
+ * with the pack rule (lorafold.cpp:138-156). The base columns do not change.
+ *   B: device fp32 [N][rank] in the projection's logical row order (up_gate: [0,F) up, [F,2F) gate).
+ *   A: device fp32 [rank][K_base] (K_base = D, or F for ffn_down).   rank 1..128.
+ * Synchronous on the handle's stream (host eigen-solves between device steps); returns HX_E_FORMAT
+ * for a weight set without LoRA slots or with non-q8 matrices. */
+HX_API int hx_lora_fold_slots(hx_handle h, int wfd, int proj, const float* B_dev, const float* A_dev, int rank,
+                              float scale);
+
 /* Apply a LoRA overlay file (blkNN.ovl written by moss/make_lora_overlay.py:54-56 and
  * moss/mossrun/lorafold.cpp:284-288: u32 n, then n records of u64 pack offset, u32 length, bytes)
  * to a block pack in host memory before hx_weights_load. All records are checked first; on a

@@ -237,6 +237,39 @@ def lora_fold_q8(u, scale, group, B, A, lscale=1.0, floor=F16_FLOOR_MOSS, k_base
     return out_u, out_s
 
 
+def fold_slots(BT, AM, keep=128):
+    """The rank-128 LoRA slot fold of the reference's fold tool (moss/mossrun/lorafold.cpp:200-284
+    `fold`), restated in numpy float64: BT [R][N] (turbo B^T rows then scaled user B^T rows), AM [R][I]
+    (turbo A rows then user A rows). Returns float32 B' [keep][N], A' [keep][I] with B'^T A' the best
+    rank-`keep` approximation of BT^T AM, singular values on the B side:
+      Gb = BT BT^T = Vb diag(lb) Vb^T, Ga = AM AM^T = Va diag(la) Va^T (eigenvalues below 1e-12 of the
+      largest dropped), core C = Sb Vb^T Va Sa = U S W^T, B' = S_k U_k^T Sb^-1 Vb^T BT,
+      A' = W_k^T Sa^-1 Va^T AM."""
+    BT = np.asarray(BT, np.float64)
+    AM = np.asarray(AM, np.float64)
+    lb, Vb = np.linalg.eigh(BT @ BT.T)
+    la, Va = np.linalg.eigh(AM @ AM.T)
+
+    def roots(lam):
+        ok = lam > lam.max() * 1e-12
+        sq = np.where(ok, np.sqrt(np.where(ok, lam, 1.0)), 0.0)
+        return sq, np.where(ok, 1.0 / np.where(ok, sq, 1.0), 0.0)
+
+    sb, ib = roots(lb)
+    sa, ia = roots(la)
+    C = (sb[:, None] * (Vb.T @ Va)) * sa[None, :]
+    U, S, Wt = np.linalg.svd(C)
+    k = min(keep, len(S))
+    S = np.where(S[:k] > S[0] * 1e-12, S[:k], 0.0)
+    Tb = (Vb * ib[None, :]) @ (U[:, :k] * S[None, :])      # [R][k]
+    Ta = Wt[:k] @ (ia[:, None] * Va.T)                      # [k][R]
+    Bo = np.zeros((keep, BT.shape[1]))
+    Ao = np.zeros((keep, AM.shape[1]))
+    Bo[:k] = Tb.T @ BT
+    Ao[:k] = Ta @ AM
+    return Bo.astype(np.float32), Ao.astype(np.float32)
+
+
 def situ_logical_rows(n_rows):
     """Device row r of a MOSS up_gate matrix -> its logical row ([0,F) up, [F,2F) gate); inverse view of situ_rows."""
     F = n_rows // 2

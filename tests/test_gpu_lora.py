@@ -162,3 +162,96 @@ def test_fold_rejects_bad_arguments(h):
         h.lora_fold(wfd + 1000, rt.W_QKV, b, a, 8, 1.0)
     assert e.value.rc == rt.HX_E_NOWEIGHTS
     h.weights_free(wfd)
+
+
+def _deq64(tu, ts, group):
+    return op.dequant_q8(tu.cpu().numpy(), ts.cpu().numpy(), group).astype(np.float64)
+
+
+def test_moss_fold_into_rank128_slots(h):
+    """hx_lora_fold_slots (the SVD fold of moss/mossrun/lorafold.cpp:200-284) on a MOSS q8 weight set with
+    LoRA slots: for every projection, the new slots' product B'^T A' against the best rank-128
+    approximation of (current slots + scale B A) from oracle.packs.fold_slots, within the q8
+    requantisation error (about 0.8 %, bar 2e-2); the base columns and the other LoRA-A rows untouched;
+    then a block on the folded weights against the oracle block (2e-3)."""
+    D, F, B, group = 256, 256, 1, 32
+    g = torch.Generator().manual_seed(70)
+    shapes = {rt.W_Q: (D, D + 128), rt.W_K: (D, D + 128), rt.W_V: (D, D + 128), rt.W_O: (D, D + 128),
+              rt.W_M1: (2 * F, D + 128), rt.W_M2: (D, F + 128), rt.W_AQKV: (384, D), rt.W_AO: (128, D),
+              rt.W_AUG: (128, D), rt.W_ADN: (128, F)}
+    mats, dv = {}, {}
+    for slot, (n, k) in shapes.items():
+        w = torch.randn(n, k, generator=g) * 0.02
+        if slot in (rt.W_Q, rt.W_K, rt.W_V, rt.W_O, rt.W_M1, rt.W_M2):
+            w[:, k - 128 + 40:] = 0  # turbo slots of effective rank 40 in the B columns
+        mats[slot], tu, ts = _q8(w.numpy(), group)
+        dv[slot] = (tu, ts)
+    gain = torch.cat((1 + 0.1 * torch.randn(128, generator=g), 1 + 0.1 * torch.randn(128, generator=g),
+                      1 + 0.1 * torch.randn(2 * D, generator=g)))
+    gain[:128] /= np.sqrt(128.0)
+    tg = gain.cuda()
+    wfd = h.weights_bind(rt.MODEL_MOSS, D, F, mats, tg, lora=1, keep=[t for p in dv.values() for t in p] + [tg])
+    table = ((rt.LORA_Q, rt.W_Q, rt.W_AQKV, 0, D, 32), (rt.LORA_K, rt.W_K, rt.W_AQKV, 128, D, 100),
+             (rt.LORA_V, rt.W_V, rt.W_AQKV, 256, D, 64), (rt.LORA_O, rt.W_O, rt.W_AO, 0, D, 128),
+             (rt.LORA_UG, rt.W_M1, rt.W_AUG, 0, D, 48), (rt.LORA_DN, rt.W_M2, rt.W_ADN, 0, F, 7))
+    scale = 0.7
+    for proj, slot, aslot, row0, kb, rank in table:
+        W0, A0 = _deq64(*dv[slot], group), _deq64(*dv[aslot], group)
+        u_base = dv[slot][0].cpu().numpy()[:, :kb].copy()
+        a_rows = dv[aslot][0].cpu().numpy().copy()
+        N = W0.shape[0]
+        Bu = (torch.randn(N, rank, generator=g) * 0.02).numpy()   # logical row order
+        Au = (torch.randn(rank, kb, generator=g) * 0.02).numpy()
+        Bd = Bu[op.situ_logical_rows(N)] if slot == rt.W_M1 else Bu  # device row order
+        BT = np.vstack((W0[:, kb:].T, scale * Bd.T.astype(np.float64)))
+        AM = np.vstack((A0[row0:row0 + 128], Au.astype(np.float64)))
+        P = BT.T @ AM
+        U, S, Vt = np.linalg.svd(P)
+        T = (U[:, :128] * S[:128]) @ Vt[:128]
+        Bo, Ao = op.fold_slots(BT, AM)
+        ub, sb = op.quant_q8(np.ascontiguousarray(Bo.T), group)
+        ua, sa = op.quant_q8(Ao, group)
+        Qo = op.dequant_q8(ub, sb, group).astype(np.float64) @ op.dequant_q8(ua, sa, group)
+        h.lora_fold_slots(wfd, proj, dev(Bu), dev(Au), rank, scale)
+        h.sync()
+        W1, A1 = _deq64(*dv[slot], group), _deq64(*dv[aslot], group)
+        Q = W1[:, kb:] @ A1[row0:row0 + 128]
+        assert rel(torch.from_numpy(Q), torch.from_numpy(T)) < 2e-2, proj
+        assert rel(torch.from_numpy(Q), torch.from_numpy(Qo)) < 2e-2, proj
+        assert np.array_equal(dv[slot][0].cpu().numpy()[:, :kb], u_base)           # base columns untouched
+        a_now = dv[aslot][0].cpu().numpy()
+        others = np.ones(a_now.shape[0], bool)
+        others[row0:row0 + 128] = False
+        assert np.array_equal(a_now[others], a_rows[others])                      # other projections' rows
+    names = {rt.W_Q: "q", rt.W_K: "k", rt.W_V: "v", rt.W_O: "o", rt.W_M1: "ug", rt.W_M2: "dn", rt.W_AQKV: "aqkv",
+             rt.W_AO: "ao", rt.W_AUG: "aug", rt.W_ADN: "adn"}
+    deq = {names[slot]: _deq(*dv[slot], group) for slot in shapes}
+    Hh, Ww, Tt = 6, 6, 20
+    nvalid = Hh * Ww + Tt
+    T = 64
+    x = torch.randn(B, T, D, generator=g) * 2
+    mod = torch.randn(6, D, generator=g) * 0.1
+    c, s = rt.rope_moss(Hh, Ww, Tt, om.bands16().numpy(), T)
+    meta, total = rt.blob_layout(rt.MODEL_MOSS, T, 0, B, D, F)
+    S = rt.S
+    meta[S["NVALID"]] = nvalid
+    bfd = h.buf_alloc(total)
+    write_f32(h, bfd, meta[S["X"]], x.numpy())
+    write_f32(h, bfd, meta[S["COS"]], c)
+    write_f32(h, bfd, meta[S["SIN"]], s)
+    h.mega_block(meta, wfd, bfd, mod=mod.numpy())
+    y = torch.from_numpy(read_f32(h, bfd, meta[S["X"]], B * T * D).reshape(B, T, D))
+    h.buf_free(bfd)
+    ref = om.block_dev(x, mod, torch.from_numpy(c), torch.from_numpy(s), deq, gain, nvalid=nvalid, lora=True)
+    assert rel(y[:, :nvalid] - x[:, :nvalid], ref[:, :nvalid] - x[:, :nvalid]) < TOL
+    # a weight set without LoRA slots is refused
+    with pytest.raises(rt.HxError) as e:
+        W, norms, modA, modB = oa.init_weights(64, D=256, F=512, Cd=128)
+        from tests.gpu_util import anima_bind
+        wfd2, _, _, keep = anima_bind(h, W, norms, modA, modB, rt.FMT_Q8, 64)
+        try:
+            h.lora_fold_slots(wfd2, rt.LORA_Q, dev(Bu[:, :1].copy()), dev(Au[:1].copy()), 1, 1.0)
+        finally:
+            h.weights_free(wfd2)
+    assert e.value.rc == rt.HX_E_FORMAT
+    h.weights_free(wfd)
