@@ -102,6 +102,11 @@ constexpr size_t kMaxGraphs = 16;  // e.g. one per denoising step of a sampler
 
 }  // namespace
 
+struct Adapter {
+  AdapterWeights w;
+  std::vector<void*> owned;
+};
+
 struct hx_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -118,6 +123,7 @@ struct hx_ctx {
   std::map<int, std::unique_ptr<Glue>> glues;
   SampleScratch ss;
   std::map<int, std::unique_ptr<MossGlue>> moss_glues;
+  std::map<int, std::unique_ptr<Adapter>> adapters;
   MossScratch ms;
   hx::SpState sp;
   std::mutex mu;
@@ -802,6 +808,8 @@ int hx_close(hx_handle hh) {
       for (void* p : kv.second->owned) cudaFree(p);
     for (auto& kv : h->moss_glues)
       for (void* p : kv.second->owned) cudaFree(p);
+    for (auto& kv : h->adapters)
+      for (void* p : kv.second->owned) cudaFree(p);
     h->ss.release();
     h->ms.release();
     cudaFree(h->status);
@@ -1268,6 +1276,79 @@ int hx_chain(hx_handle hh, const int32_t* meta, int nmeta, const int* wfds, int 
 }
 
 // ---------------------------------------------------------------- glue + sampler
+int hx_adapter_load(hx_handle hh, const hx_anima_adapter_desc* d, int* afd) {
+  hx_ctx* h = H(hh);
+  if (!h || !d || !afd || !d->embed || d->vocab <= 0 || !d->out_w || !d->out_b || !d->norm) return HX_E_ARG;
+  for (const hx_adapter_block_desc& b : d->blocks) {
+    const void* p[] = {b.norm_sa, b.sa_q, b.sa_k, b.sa_v, b.sa_o, b.sa_qn, b.sa_kn, b.norm_ca, b.ca_q, b.ca_k,
+                       b.ca_v, b.ca_o, b.ca_qn, b.ca_kn, b.norm_mlp, b.mlp0_w, b.mlp0_b, b.mlp2_w, b.mlp2_b};
+    for (const void* q : p)
+      if (!q) return HX_E_ARG;
+  }
+  std::lock_guard<std::mutex> lk(h->mu);
+  DevGuard g(h->device);
+  auto A = std::make_unique<Adapter>();
+  bool ok = true;
+  auto copy = [&](const void* src, size_t elems) -> const __half* {
+    void* p = nullptr;
+    if (!ok || cudaMalloc(&p, elems * 2) != cudaSuccess) {
+      ok = false;
+      return nullptr;
+    }
+    A->owned.push_back(p);
+    if (cudaMemcpyAsync(p, src, elems * 2, cudaMemcpyDeviceToDevice, h->stream) != cudaSuccess) ok = false;
+    return static_cast<const __half*>(p);
+  };
+  const size_t D = 1024, F = 4096;
+  A->w.vocab = d->vocab;
+  A->w.embed = copy(d->embed, static_cast<size_t>(d->vocab) * D);
+  for (int i = 0; i < 6; ++i) {
+    const hx_adapter_block_desc& b = d->blocks[i];
+    AdapterWeights::Block& o = A->w.blocks[i];
+    o.norm_sa = copy(b.norm_sa, D);
+    o.sa_q = copy(b.sa_q, D * D);
+    o.sa_k = copy(b.sa_k, D * D);
+    o.sa_v = copy(b.sa_v, D * D);
+    o.sa_o = copy(b.sa_o, D * D);
+    o.sa_qn = copy(b.sa_qn, 64);
+    o.sa_kn = copy(b.sa_kn, 64);
+    o.norm_ca = copy(b.norm_ca, D);
+    o.ca_q = copy(b.ca_q, D * D);
+    o.ca_k = copy(b.ca_k, D * D);
+    o.ca_v = copy(b.ca_v, D * D);
+    o.ca_o = copy(b.ca_o, D * D);
+    o.ca_qn = copy(b.ca_qn, 64);
+    o.ca_kn = copy(b.ca_kn, 64);
+    o.norm_mlp = copy(b.norm_mlp, D);
+    o.mlp0_w = copy(b.mlp0_w, F * D);
+    o.mlp0_b = copy(b.mlp0_b, F);
+    o.mlp2_w = copy(b.mlp2_w, D * F);
+    o.mlp2_b = copy(b.mlp2_b, D);
+  }
+  A->w.out_w = copy(d->out_w, D * D);
+  A->w.out_b = copy(d->out_b, D);
+  A->w.norm = copy(d->norm, D);
+  if (!ok || cudaStreamSynchronize(h->stream) != cudaSuccess) {
+    for (void* p : A->owned) cudaFree(p);
+    return HX_E_CUDA;
+  }
+  *afd = h->next_fd++;
+  h->adapters[*afd] = std::move(A);
+  return HX_OK;
+}
+
+int hx_anima_adapter(hx_handle hh, int afd, const float* hidden, int S, const int32_t* ids, const float* wts, int L,
+                     float* out) {
+  hx_ctx* h = H(hh);
+  if (!h || !hidden || !ids || !wts || !out) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  auto it = h->adapters.find(afd);
+  if (it == h->adapters.end()) return HX_E_ARG;
+  DevGuard g(h->device);
+  const cudaError_t e = adapter_run(it->second->w, hidden, S, ids, wts, L, out, h->status, h->stream);
+  return e == cudaSuccess ? HX_OK : e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA;
+}
+
 int hx_glue_load(hx_handle hh, const hx_anima_glue_desc* d, int* gfd) {
   hx_ctx* h = H(hh);
   if (!h || !d || !gfd || d->D <= 0 || d->D % 256) return HX_E_ARG;

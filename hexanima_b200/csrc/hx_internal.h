@@ -121,6 +121,21 @@ cudaError_t repack_tiles_launch(const uint8_t* rec, int nb, int kb, bool q8, voi
 // (lora.cu). row_mode 1: MOSS up_gate device row order; floor_mode 0 MOSS, 1 Anima scale floor.
 cudaError_t lora_fold_launch(const DevMat& W, int k_base, const float* B, const float* A, int rank, float lscale,
                              int row_mode, int floor_mode, cudaStream_t s);
+// The Anima LLM adapter (adapter.cu): fp16 device weights, 6 blocks.
+struct AdapterWeights {
+  const __half* embed = nullptr;  // [vocab][1024]
+  int vocab = 0;
+  struct Block {
+    const __half *norm_sa, *sa_q, *sa_k, *sa_v, *sa_o, *sa_qn, *sa_kn;
+    const __half *norm_ca, *ca_q, *ca_k, *ca_v, *ca_o, *ca_qn, *ca_kn;
+    const __half *norm_mlp, *mlp0_w, *mlp0_b, *mlp2_w, *mlp2_b;
+  } blocks[6];
+  const __half *out_w = nullptr, *out_b = nullptr, *norm = nullptr;
+};
+// hidden fp32 [S][1024] on the device, ids / wts on the host ([L], L <= 512), out fp32 [512][1024] on the
+// device; synchronous on s
+cudaError_t adapter_run(const AdapterWeights& W, const float* hidden, int S, const int32_t* ids_host,
+                        const float* wts_host, int L, float* out, int* status, cudaStream_t s);
 // the rank-128 LoRA slot fold (lorasvd.cu): W the LoRA-carrying matrix (K = k_base + 128), A the
 // LoRA-A matrix whose rows a_row0 .. +127 are the slots; synchronous on s
 cudaError_t lora_fold_slots(const DevMat& W, int k_base, int row_mode, const DevMat& A, int a_row0, const float* Bu,

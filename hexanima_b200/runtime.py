@@ -73,6 +73,19 @@ class hx_weight_desc(ctypes.Structure):
                 ("modA", ctypes.c_void_p), ("modB", ctypes.c_void_p)]
 
 
+ADAPTER_BLOCK_KEYS = ("norm_sa", "sa_q", "sa_k", "sa_v", "sa_o", "sa_qn", "sa_kn", "norm_ca", "ca_q", "ca_k", "ca_v",
+                      "ca_o", "ca_qn", "ca_kn", "norm_mlp", "mlp0_w", "mlp0_b", "mlp2_w", "mlp2_b")
+
+
+class hx_adapter_block_desc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ADAPTER_BLOCK_KEYS]
+
+
+class hx_anima_adapter_desc(ctypes.Structure):
+    _fields_ = [("embed", ctypes.c_void_p), ("vocab", ctypes.c_int), ("blocks", hx_adapter_block_desc * 6),
+                ("out_w", ctypes.c_void_p), ("out_b", ctypes.c_void_p), ("norm", ctypes.c_void_p)]
+
+
 class hx_anima_glue_desc(ctypes.Structure):
     _fields_ = [("D", ctypes.c_int), ("t_norm", ctypes.c_void_p), ("t_lin1", ctypes.c_void_p),
                 ("t_lin2", ctypes.c_void_p), ("x_emb", ctypes.c_void_p), ("f_modA", ctypes.c_void_p),
@@ -134,6 +147,8 @@ _SIGS = {
     "hx_modulation_noalloc": [_vp, _vp, _vp, _vp, _vp, _i, _i, _vp],
     "hx_chain": [_vp, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _vp, _vp, ctypes.c_uint32, _i, _ip],
     "hx_glue_load": [_vp, ctypes.POINTER(hx_anima_glue_desc), ctypes.POINTER(_i)],
+    "hx_adapter_load": [_vp, ctypes.POINTER(hx_anima_adapter_desc), ctypes.POINTER(_i)],
+    "hx_anima_adapter": [_vp, _i, _vp, _i, _vp, _vp, _i, _vp],
     "hx_anima_sample": [_vp, _i, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _i, _i, _i, _vp, _i, _ip],
     "hx_moss_glue_load": [_vp, ctypes.POINTER(hx_moss_glue_desc), ctypes.POINTER(_i)],
     "hx_mgl1_tensor": [_vp, _sz, ctypes.c_char_p, ctypes.POINTER(_i), ctypes.POINTER(_i), _ip, ctypes.POINTER(_vp),
@@ -368,6 +383,28 @@ class Handle:
         g = ctypes.c_int()
         _check(lib().hx_glue_load(self.h, ctypes.byref(d), ctypes.byref(g)), "hx_glue_load")
         return g.value
+
+    def adapter_load(self, W):
+        """W: device fp16 tensors {"embed" [vocab][1024], "blocks": 6 dicts of ADAPTER_BLOCK_KEYS, "out_w", "out_b",
+        "norm"} (copied into handle-owned memory)."""
+        d = hx_anima_adapter_desc()
+        d.embed = _ptr(W["embed"])
+        d.vocab = int(W["embed"].shape[0])
+        for i, b in enumerate(W["blocks"]):
+            for k in ADAPTER_BLOCK_KEYS:
+                setattr(d.blocks[i], k, _ptr(b[k]))
+        d.out_w, d.out_b, d.norm = _ptr(W["out_w"]), _ptr(W["out_b"]), _ptr(W["norm"])
+        a = ctypes.c_int()
+        _check(lib().hx_adapter_load(self.h, ctypes.byref(d), ctypes.byref(a)), "hx_adapter_load")
+        return a.value
+
+    def anima_adapter(self, afd, hidden_dev, ids, wts, out_dev):
+        """Context [512][1024] fp32 into out_dev from hidden_dev fp32 [S][1024] and host ids / wts [L]."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        wts = np.ascontiguousarray(wts, np.float32)
+        S = int(hidden_dev.shape[0])
+        _check(lib().hx_anima_adapter(self.h, afd, _ptr(hidden_dev), S, ids.ctypes.data, wts.ctypes.data, len(ids),
+                                      _ptr(out_dev)), "hx_anima_adapter")
 
     def anima_sample(self, gfd, meta, wfds, bfd, latent_dev, lat_h, lat_w, nsteps=4, sigmas=None, use_graph=True):
         m = (ctypes.c_int32 * len(meta))(*meta)

@@ -282,6 +282,44 @@ HX_API int hx_anima_sample(hx_handle h, int gfd, const int32_t* meta, int nmeta,
                            float* latent_dev, int lat_h, int lat_w, int nsteps, const float* sigmas, int use_graph,
                            int32_t* rc);
 
+/* The Anima LLM adapter (phone/animad.cpp:179-218): 6 blocks (dim 1024, 16 heads x 64, MLP 4096) that turn
+ * T5 token ids and the LLM's hidden states into the DiT cross-attention context. Weights: fp16 device
+ * arrays, names as in the checkpoint (llm_adapter.*); copied by hx_adapter_load. */
+typedef struct {
+  const void* norm_sa;  /* [1024] norm_self_attn.weight */
+  const void* sa_q;     /* [1024][1024] self_attn.q_proj.weight (k_proj, v_proj, o_proj alike) */
+  const void* sa_k;
+  const void* sa_v;
+  const void* sa_o;
+  const void* sa_qn;    /* [64] self_attn.q_norm.weight */
+  const void* sa_kn;    /* [64] self_attn.k_norm.weight */
+  const void* norm_ca;  /* [1024] norm_cross_attn.weight */
+  const void* ca_q;     /* cross_attn.{q,k,v,o}_proj.weight [1024][1024] */
+  const void* ca_k;
+  const void* ca_v;
+  const void* ca_o;
+  const void* ca_qn;    /* [64] */
+  const void* ca_kn;    /* [64] */
+  const void* norm_mlp; /* [1024] */
+  const void* mlp0_w;   /* [4096][1024] mlp.0.weight */
+  const void* mlp0_b;   /* [4096] */
+  const void* mlp2_w;   /* [1024][4096] mlp.2.weight */
+  const void* mlp2_b;   /* [1024] */
+} hx_adapter_block_desc;
+typedef struct {
+  const void* embed;    /* [vocab][1024] llm_adapter.embed.weight */
+  int vocab;
+  hx_adapter_block_desc blocks[6];
+  const void* out_w;    /* [1024][1024] out_proj.weight */
+  const void* out_b;    /* [1024] out_proj.bias */
+  const void* norm;     /* [1024] norm.weight */
+} hx_anima_adapter_desc;
+HX_API int hx_adapter_load(hx_handle h, const hx_anima_adapter_desc* d, int* afd);
+/* Context [512][1024] fp32 (device, rows >= L zero) from hidden fp32 [S][1024] (device), token ids
+ * int32 [L] and per-token weights fp32 [L] (host; 1 <= L <= 512, 0 <= id < vocab). Synchronous. */
+HX_API int hx_anima_adapter(hx_handle h, int afd, const float* hidden_dev, int S, const int32_t* ids, const float* wts,
+                            int L, float* out_dev);
+
 /* MOSS sampler glue (moss/sample_ref.py:14-20 with moss_ref.py:96-120 dit_forward; mossrun.cpp:306-333):
  * weights as device arrays (copied), fp16 matrices and fp32 vectors, moss_ref names. */
 typedef struct {

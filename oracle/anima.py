@@ -226,3 +226,92 @@ def sample(lat, ctx, cos, sin, blocks, glue, steps=4, sigmas=None):
         v = unpatchify(h @ glue["f_lin"].float().T, H, Wd)
         lat = lat + (float(sig[i + 1]) - float(sig[i])) * v
     return lat
+
+
+# ---------------------------------------------------------------- LLM adapter (text side)
+ADAPTER_DIM, ADAPTER_HEADS, ADAPTER_HD, ADAPTER_FF, ADAPTER_BLOCKS, ADAPTER_CTX = 1024, 16, 64, 4096, 6, 512
+ADAPTER_BLOCK_KEYS = ("norm_sa", "sa_q", "sa_k", "sa_v", "sa_o", "sa_qn", "sa_kn", "norm_ca", "ca_q", "ca_k", "ca_v",
+                      "ca_o", "ca_qn", "ca_kn", "norm_mlp", "mlp0_w", "mlp0_b", "mlp2_w", "mlp2_b")
+
+
+def adapter_rope(n, hd=ADAPTER_HD):
+    """1D split-half RoPE tables [n][hd/2] (phone/animad.cpp:130-137 `rope1d`): angle i / 10000^(2j/hd),
+    in float64, rounded to float32."""
+    j = np.arange(hd // 2, dtype=np.float64)
+    a = np.arange(n, dtype=np.float64)[:, None] / np.power(10000.0, 2.0 * j / hd)[None, :]
+    return torch.from_numpy(np.cos(a).astype(np.float32)), torch.from_numpy(np.sin(a).astype(np.float32))
+
+
+def _adapter_rms(x, g, eps=1e-6):
+    return x * torch.rsqrt((x.double() ** 2).mean(-1, keepdim=True).float() + eps) * g
+
+
+def _adapter_rope(t, c, s):
+    """t [n, heads, 64]: pairs (j, j+32) rotated (animad.cpp:138-148 `rope_apply`)."""
+    a, b = t[..., :32], t[..., 32:]
+    c, s = c[:, None, :], s[:, None, :]
+    return torch.cat((a * c - b * s, a * s + b * c), -1)
+
+
+def adapter(hidden, ids, wts, W):
+    """The Anima LLM adapter (phone/animad.cpp:179-218): T5 token ids [L] and LLM hidden states
+    hidden [S][1024] -> cross-attention context [512][1024] (rows >= L zero). Six blocks of
+    RMS -> self-attention (16 heads x 64, per-head RMS on q/k, 1D RoPE) -> RMS -> cross-attention to
+    hidden (keys roped with their own positions) -> RMS -> MLP 1024 -> 4096 (GELU erf) -> 1024, each
+    adding into x; then out_proj, RMS (norm) and a per-token weight. Float32 math on fp16 weights;
+    W holds fp32 copies of the fp16 weights: "embed", "blocks" (list of dicts with ADAPTER_BLOCK_KEYS),
+    "out_w", "out_b", "norm"."""
+    L, S = len(ids), hidden.shape[0]
+    H, hd = ADAPTER_HEADS, ADAPTER_HD
+    x = W["embed"][torch.as_tensor(ids, dtype=torch.long)].clone()
+    tc, ts = adapter_rope(L)
+    sc, ss = adapter_rope(S)
+
+    def attn(Bw, pre, xq, xkv, cross):
+        q = (xq @ Bw[pre + "_q"].T).view(-1, H, hd)
+        k = (xkv @ Bw[pre + "_k"].T).view(-1, H, hd)
+        v = (xkv @ Bw[pre + "_v"].T).view(-1, H, hd)
+        q = _adapter_rope(_adapter_rms(q, Bw[pre + "_qn"]), tc, ts)
+        k = _adapter_rope(_adapter_rms(k, Bw[pre + "_kn"]), sc if cross else tc, ss if cross else ts)
+        p = torch.softmax(torch.einsum("qhd,khd->hqk", q, k) * 0.125, -1)
+        o = torch.einsum("hqk,khd->qhd", p, v).reshape(-1, H * hd)
+        return o @ Bw[pre + "_o"].T
+
+    for Bw in W["blocks"]:
+        h = _adapter_rms(x, Bw["norm_sa"])
+        x = x + attn(Bw, "sa", h, h, False)
+        h = _adapter_rms(x, Bw["norm_ca"])
+        x = x + attn(Bw, "ca", h, hidden, True)
+        h = _adapter_rms(x, Bw["norm_mlp"])
+        m = gelu(h @ Bw["mlp0_w"].T + Bw["mlp0_b"])
+        x = x + (m @ Bw["mlp2_w"].T + Bw["mlp2_b"])
+    y = _adapter_rms(x @ W["out_w"].T + W["out_b"], W["norm"]) * torch.as_tensor(wts, dtype=torch.float32)[:, None]
+    out = torch.zeros(ADAPTER_CTX, ADAPTER_DIM)
+    out[:L] = y
+    return out
+
+
+def adapter_init(seed, vocab=1000, std=0.02):
+    """Seeded synthetic adapter weights, fp16-representable (returned as fp16 tensors)."""
+    g = torch.Generator().manual_seed(seed)
+    D, F = ADAPTER_DIM, ADAPTER_FF
+    n = lambda *s: (torch.randn(*s, generator=g) * std).half()
+    gn = lambda d: (1 + 0.1 * torch.randn(d, generator=g)).half()
+    blocks = []
+    for _ in range(ADAPTER_BLOCKS):
+        b = {}
+        for pre in ("sa", "ca"):
+            for m in ("q", "k", "v", "o"):
+                b[f"{pre}_{m}"] = n(D, D)
+            b[f"{pre}_qn"], b[f"{pre}_kn"] = gn(ADAPTER_HD), gn(ADAPTER_HD)
+        b["norm_sa"], b["norm_ca"], b["norm_mlp"] = gn(D), gn(D), gn(D)
+        b["mlp0_w"], b["mlp0_b"], b["mlp2_w"], b["mlp2_b"] = n(F, D), n(F), n(D, F), n(D)
+        blocks.append(b)
+    return {"embed": (torch.randn(vocab, D, generator=g)).half(), "blocks": blocks, "out_w": n(D, D), "out_b": n(D),
+            "norm": gn(D)}
+
+
+def adapter_f32(W16):
+    """fp32 copies of fp16 adapter weights (the arithmetic the reference does on them)."""
+    return {"embed": W16["embed"].float(), "blocks": [{k: v.float() for k, v in b.items()} for b in W16["blocks"]],
+            "out_w": W16["out_w"].float(), "out_b": W16["out_b"].float(), "norm": W16["norm"].float()}
