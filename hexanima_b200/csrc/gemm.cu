@@ -51,6 +51,7 @@ struct KParams {
   int M, N, nkb, nkb1, group;
   int num_m_tiles, num_tiles;
   int num_n_tiles, n_fastest;  // tile order: n_fastest walks the N tiles of one M block consecutively
+  int ksplit;                  // split-K (residual epilogue only): work unit t covers K slice t / (M x N tiles)
   __half* out;
   int ldo;
   float* x;
@@ -67,12 +68,20 @@ struct KParams {
   int* status;
 };
 
-// tile t -> (M tile, N tile) in the launch's order
+// work unit t -> (M tile, N tile) in the launch's order, and its K-block range [kb0, kb1): with split-K
+// the units of K slice j are t in [j, j + 1) x (M tiles x N tiles), each reduce-adding a partial sum
 __device__ __forceinline__ int tile_m(const KParams& p, int t) {
+  t %= p.num_m_tiles * p.num_n_tiles;
   return p.n_fastest ? t / p.num_n_tiles : t % p.num_m_tiles;
 }
 __device__ __forceinline__ int tile_n(const KParams& p, int t) {
+  t %= p.num_m_tiles * p.num_n_tiles;
   return p.n_fastest ? t % p.num_n_tiles : t / p.num_m_tiles;
+}
+__device__ __forceinline__ void kb_range(const KParams& p, int t, int& kb0, int& kb1) {
+  const int per = (p.nkb + p.ksplit - 1) / p.ksplit;
+  kb0 = (t / (p.num_m_tiles * p.num_n_tiles)) * per;
+  kb1 = min(p.nkb, kb0 + per);
 }
 
 // ---------------------------------------------------------------- dequantisers
@@ -522,7 +531,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
         const int t = blockIdx.x + ti * gridDim.x;
         const int m0 = tile_m(p, t) * BM, n0 = tile_n(p, t) * BN;
-        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        int kb0, kb1;
+        kb_range(p, t, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.status, 101)) { ok = false; break; }
@@ -553,7 +564,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(&tempty[acc], ((ti >> 1) & 1) ^ 1, p.status, 102)) { ok = false; break; }
         tc_fence_after();
         const uint32_t dt = tmem + acc * BN;
-        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        int kb0, kb1;
+        kb_range(p, blockIdx.x + ti * gridDim.x, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&full[s], ph, p.status, 103)) { ok = false; break; }
@@ -565,7 +578,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             mma_f16_ss(dt, sdesc_sw128(a0 + 32 * k, 16, 1024), sdesc_sw128(b0 + 32 * k, 16, 1024), idesc,
-                       (kb | k) != 0);
+                       (kb != kb0 || k != 0));
           }
           issued = true;
           mma_commit(&empty[s]);
@@ -584,7 +597,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
-        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        int kb0, kb1;
+        kb_range(p, blockIdx.x + ti * gridDim.x, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&full[s], ph, p.status, 105)) { ok = false; break; }
@@ -725,7 +740,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
         const int t = pair + ti * npairs;
         const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * BN + row0;
-        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        int kb0, kb1;
+        kb_range(p, t, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.status, 111)) { ok = false; break; }
@@ -755,7 +772,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(&tempty[acc], ((ti >> 1) & 1) ^ 1, p.status, 112)) { ok = false; break; }
         tc_fence_after();
         const uint32_t dt = tmem + acc * BN;
-        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        int kb0, kb1;
+        kb_range(p, pair + ti * npairs, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&full_a[s], ph, p.status, 113)) { ok = false; break; }
@@ -767,7 +786,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             mma_f16_ss_pair(dt, sdesc_sw128(a0 + 32 * k, 16, 1024), sdesc_sw128(b0 + 32 * k, 16, 1024), idesc,
-                            (kb | k) != 0);
+                            (kb != kb0 || k != 0));
           issued = true;
           mma_commit_pair_mc(&empty[s], 0x3);
         }
@@ -785,7 +804,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
-        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
+        int kb0, kb1;
+        kb_range(p, pair + ti * npairs, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&raw_full[s], ph, p.status, 115)) { ok = false; break; }
@@ -981,11 +1002,34 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   if (a.tile == 0 && a.epi == EPI_RMS && gemm_wt_eligible(a) && gemm_wt_tiles(a) >= sm_count() / 2)
     return gemm_wt_launch(a, s);
 
-  // tile configuration: CTA pairs (256x256 per cluster) when there are enough pair tiles to fill the
-  // GPU (M1 shape, 8 images: q8 1098 vs 869 TFLOP/s, fp16 1230 vs 1160), else single-CTA 128x256
-  // tiles (small M: the context GEMM, one image)
+  // tile configuration: CTA pairs (256x256 per cluster) unless single-CTA 128x256 tiles need fewer waves
+  // (a pair moves half the weight tile per SM, so at equal waves it is the faster of the two: at one
+  // image the down projection runs 67 us in pairs against 86 us in single CTAs)
   const int pair_tiles = ((a.M + 2 * HALF - 1) / (2 * HALF)) * ((N + BN - 1) / BN);
-  const bool pair = a.tile == 2 || (a.tile == 0 && pair_tiles >= sm_count() / 2);
+  const int single_tiles = ((a.M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  bool pair = a.tile == 2 || (a.tile == 0 && (pair_tiles + sm_count() / 2 - 1) / (sm_count() / 2) <=
+                                                 (single_tiles + sm_count() - 1) / sm_count());
+  // residual GEMMs with few tiles (one or two images per GPU): split K so that the work units fill the
+  // GPU; each unit reduce-adds its partial product into x (the sum order of the slices is not fixed).
+  // Model: waves x (k-blocks per unit + a fixed cost per unit for pipeline fill and epilogue), CTA pairs
+  // about 15 % faster per k-block than single CTAs; a split must promise at least 8 %.
+  int ksplit = 1;
+  if (a.epi == EPI_RESID && a.tile == 0 && a.max_ctas == 0) {
+    const int nkb = K / BK, nsm = sm_count(), npairs = nsm / 2;
+    constexpr double kUnitCost = 8.0;
+    auto waves = [](long units, long slots) { return static_cast<double>((units + slots - 1) / slots); };
+    double best = (pair ? waves(pair_tiles, npairs) : 1.15 * waves(single_tiles, nsm)) * (nkb + kUnitCost);
+    for (int ks = 2; ks <= 4; ++ks) {
+      const int per = (nkb + ks - 1) / ks;
+      if (per < 8 || (ks - 1) * per >= nkb) break;
+      const double c = waves(static_cast<long>(pair_tiles) * ks, npairs) * (per + kUnitCost);
+      if (c < 0.92 * best) {
+        best = c;
+        ksplit = ks;
+        pair = true;
+      }
+    }
+  }
   const uint32_t wrows = pair ? HALF : BN;
 
   CUtensorMap tA, tA2, tW, tS, tMin, tX;
@@ -1036,7 +1080,8 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   p.group = W->fmt == WF_F16 ? 64 : W->group;
   p.num_m_tiles = pair ? (a.M + 2 * HALF - 1) / (2 * HALF) : (a.M + BM - 1) / BM;
   p.num_n_tiles = (N + BN - 1) / BN;
-  p.num_tiles = p.num_m_tiles * p.num_n_tiles;
+  p.ksplit = ksplit;
+  p.num_tiles = p.num_m_tiles * p.num_n_tiles * ksplit;
   // default order walks M tiles under one weight block (the weight block stays in L2); when the A
   // operand is far larger than L2 but the weights fit (the mlp down projection reading the 8-image
   // hidden state), walk the N tiles of one A block instead so A streams from HBM once

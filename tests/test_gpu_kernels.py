@@ -112,6 +112,23 @@ def test_gemm_residual(h, tile):
     assert rel(x.cpu() - x0, ref - x0) < 2e-3
 
 
+@pytest.mark.parametrize("M,K", [(1536, 8192), (3072, 2048)])
+def test_gemm_residual_split_k(h, M, K):
+    """One / two images of the residual down- and o-projection shapes: the automatic choice splits K over
+    CTA-pair work units that reduce-add partial sums into x (fp32 sums in an unfixed order)."""
+    torch.manual_seed(31)
+    N, T = 2048, 1536
+    A = (torch.randn(M, K) * 0.5).half()
+    mat, keep, Wd = make_mat(rt.FMT_Q8, (torch.randn(N, K) * 0.02).numpy(), 64)
+    x0 = torch.randn(M, N)
+    gate = torch.randn(M // T, N)
+    x = x0.cuda()
+    h.gemm(A.cuda(), M, mat, rt.EPI_RESID, lda=K, x=x, ldx=N, gate=gate.cuda(), vec_bstride=N, rows_per_img=T)
+    h.sync()
+    ref = x0 + gate.repeat_interleave(T, 0) * _ref_gemm(A, Wd)
+    assert rel(x.cpu() - x0, ref - x0) < 2e-3
+
+
 @pytest.mark.parametrize("tile", TILES3)
 def test_gemm_large_a_operand(h, tile):
     """A larger than L2 (134 MB) with small weights: the launch walks the N tiles of each A block
