@@ -86,8 +86,11 @@ struct SampleScratch {
   float *tp = nullptr, *emb = nullptr, *tmp = nullptr, *lora = nullptr, *h256 = nullptr, *fmod = nullptr,
         *y = nullptr;
   __half* P = nullptr;
+  __half* ckv = nullptr;  // cross-attention k|v of every block, computed once per sample
+  size_t ckv_elems = 0;
   void release() {
-    for (void* p : {(void*)tp, (void*)emb, (void*)tmp, (void*)lora, (void*)h256, (void*)fmod, (void*)y, (void*)P})
+    for (void* p : {(void*)tp, (void*)emb, (void*)tmp, (void*)lora, (void*)h256, (void*)fmod, (void*)y, (void*)P,
+                    (void*)ckv})
       cudaFree(p);
     *this = SampleScratch();
   }
@@ -341,6 +344,7 @@ struct Stage {
   int ti = 0;
   int stop;
   bool stopped = false;
+  const __half* ckv_pre = nullptr;  // Anima: this block's cross-attention k|v already computed (sampler cache)
   // returns true when the caller must stop (meta STOP reached)
   bool tick() {
     if (ntimes > 0 && ti < 32) cudaEventRecord(h->ev[ti + 1], h->stream);
@@ -373,6 +377,16 @@ GemmArgs gargs(hx_ctx* h, const __half* A, int lda, int M, const DevMat* W, int 
   g.epi = epi;
   g.status = h->status;
   return g;
+}
+
+// cross-attention k|v of one Anima block: [rows][2D] fp16, k RMS-normalised with the ck gain
+cudaError_t ckv_launch(hx_ctx* h, const Weights& W, const __half* ctx, int rows, __half* out) {
+  GemmArgs gk = gargs(h, ctx, W.Cd, rows, &W.mats[HX_W_CKV], EPI_RMS);
+  gk.out = out;
+  gk.ldo = 2 * W.D;
+  gk.gain0 = W.gain + 384;
+  gk.seg1 = gk.seg2 = W.D;
+  return gemm_launch(gk, h->stream);
 }
 
 int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, const float* mod, Stage& st) {
@@ -434,12 +448,11 @@ int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob,
       gq.gain0 = gain + 256;
       gq.seg1 = gq.seg2 = D;
       CKL(gemm_launch(gq, s));
-      GemmArgs gk = gargs(h, ctx, Cd, B * C, &W.mats[HX_W_CKV], EPI_RMS);
-      gk.out = ckv;
-      gk.ldo = 2 * D;
-      gk.gain0 = gain + 384;
-      gk.seg1 = gk.seg2 = D;
-      CKL(gemm_launch(gk, s));
+      if (st.ckv_pre) {
+        ckv = const_cast<__half*>(st.ckv_pre);
+      } else {
+        CKL(ckv_launch(h, W, ctx, B * C, ckv));
+      }
       if (st.tick()) return HX_OK;
       if (st.tick()) return HX_OK;  // rms slot: fused into the two GEMMs above
       AttnArgs a;
@@ -691,7 +704,8 @@ constexpr size_t kModStride(int D) { return 9ull * D + 3 * 256; }
 // mods_dev: per-block device mod vectors, block k at mods_dev + k * mod_stride (stride 0: one shared vector,
 // as MOSS blocks use); NULL computes them from emb / lora with each block's AdaLN weights.
 int chain_body(hx_ctx* h, const std::vector<const Weights*>& ws, const int32_t* m, uint8_t* blob, const float* mods_dev,
-               const float* emb_dev, const float* lora_dev, uint32_t skipmask, size_t mod_stride) {
+               const float* emb_dev, const float* lora_dev, uint32_t skipmask, size_t mod_stride,
+               const __half* ckv_cache = nullptr, size_t ckv_stride = 0) {
   const int model = ws[0]->model, D = ws[0]->D;
   const size_t per = model == HX_MODEL_ANIMA ? kModStride(D) : 6ull * D;
   for (size_t k = 0; k < ws.size(); ++k) {
@@ -707,6 +721,7 @@ int chain_body(hx_ctx* h, const std::vector<const Weights*>& ws, const int32_t* 
       md = out;
     }
     Stage st{h, 0, 0, 0};
+    if (ckv_cache) st.ckv_pre = ckv_cache + k * ckv_stride;
     if (int r = run_block(h, *ws[k], m, blob, md, st)) return r;
   }
   return HX_OK;
@@ -1431,8 +1446,10 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
   for (int i = 0; i < nsteps; ++i) sg.s[i] = sig[i];
   DevGuard g(h->device);
   const size_t rows = static_cast<size_t>(B) * T;
+  const int C = m[HX_A_NCTX];
+  const size_t ckv_stride = static_cast<size_t>(B) * C * 2 * D, ckv_need = ckv_stride * nblk;
   SampleScratch& sc = h->ss;
-  if (sc.S < nsteps || sc.D != D || sc.rows < rows) {
+  if (sc.S < nsteps || sc.D != D || sc.rows < rows || sc.ckv_elems < ckv_need) {
     cudaStreamSynchronize(h->stream);
     h->drop_graphs();
     sc.release();
@@ -1440,7 +1457,8 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
     bool ok = cudaMalloc(&sc.tp, S * D * 4) == cudaSuccess && cudaMalloc(&sc.emb, S * D * 4) == cudaSuccess &&
               cudaMalloc(&sc.tmp, S * D * 4) == cudaSuccess && cudaMalloc(&sc.lora, S * 3 * D * 4) == cudaSuccess &&
               cudaMalloc(&sc.h256, S * 256 * 4) == cudaSuccess && cudaMalloc(&sc.fmod, S * 2 * D * 4) == cudaSuccess &&
-              cudaMalloc(&sc.y, rows * 64 * 4) == cudaSuccess && cudaMalloc(&sc.P, rows * 128 * 2) == cudaSuccess;
+              cudaMalloc(&sc.y, rows * 64 * 4) == cudaSuccess && cudaMalloc(&sc.P, rows * 128 * 2) == cudaSuccess &&
+              cudaMalloc(&sc.ckv, ckv_need * 2) == cudaSuccess;
     if (!ok) {
       sc.release();
       return (*rc = HX_E_CUDA);
@@ -1448,10 +1466,12 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
     sc.S = static_cast<int>(S);
     sc.D = D;
     sc.rows = rows;
+    sc.ckv_elems = ckv_need;
   }
   if (int r = ensure_modscratch(h, kModStride(D) * nblk)) return (*rc = r);
   uint8_t* blob = static_cast<uint8_t*>(bi->second.ptr);
   float* x = reinterpret_cast<float*>(blob + m[HX_A_X]);
+  const __half* ctxp = hptr(blob, m[HX_A_CTX]);
   __half* hbuf = hptr(blob, m[HX_A_H]);
   cudaStream_t s = h->stream;
   auto body = [&]() -> int {
@@ -1461,6 +1481,8 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
     CKL(gemv_rows_launch(G.t_lin2, sc.tmp, sc.lora, S, D, 3 * D, 1, nullptr, 0, 3 * D, s));
     CKL(gemv_rows_launch(G.f_modA, sc.emb, sc.h256, S, D, 256, 1, nullptr, 0, 256, s));
     CKL(gemv_rows_launch(G.f_modB, sc.h256, sc.fmod, S, 256, 2 * D, 0, sc.lora, 3 * D, 2 * D, s));
+    // the cross-attention k|v of each block depend only on the context: once per sample, not per step
+    for (int k = 0; k < nblk; ++k) CKL(ckv_launch(h, *ws[k], ctxp, B * C, sc.ckv + k * ckv_stride));
     DevMat xe, fl;
     xe.fmt = WF_F16; xe.N = D; xe.K = 128; xe.w = G.x_emb;
     fl.fmt = WF_F16; fl.N = 64; fl.K = D; fl.w = G.f_lin;
@@ -1471,7 +1493,7 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
       ge.ldx = D;
       CKL(gemm_launch(ge, s));
       if (int r = chain_body(h, ws, m.data(), blob, nullptr, sc.emb + static_cast<size_t>(i) * D,
-                             sc.lora + static_cast<size_t>(i) * 3 * D, 0, 0))
+                             sc.lora + static_cast<size_t>(i) * 3 * D, 0, 0, sc.ckv, ckv_stride))
         return r;
       const float* fm = sc.fmod + static_cast<size_t>(i) * 2 * D;
       CKL(lnmod_launch(x, hbuf, static_cast<int>(rows), D, fm, fm + D, 0, T, 1e-6f, s));
