@@ -333,8 +333,10 @@ def run_ours(args, rank, world, local_rank):
     # roofline: the dominant q8 GEMM alone, live
     tf, gms = time_q8_gemm(h, rt, torch, dev, B * T)
     traffic = _profile_traffic()
-    launches_per_block = 3 + 7 + 2 + 2  # LN x3, GEMM x7, attention x2, modulation mat-vecs x2
-    launches_per_sample = 5 + NSTEP * (5 + launches_per_block * NBLK)  # temb + 4 mat-vecs; per step glue + blocks
+    launches_per_block = 3 + 6 + 2  # LN x3, GEMM x6 (the cross-attention k|v GEMM runs once per sample), attention x2
+    # temb + 4 mat-vecs and one k|v GEMM per block once per sample; per step: 5 glue launches, the blocks'
+    # modulation batched in 3 launches, and the blocks
+    launches_per_sample = 5 + NBLK + NSTEP * (5 + 3 + launches_per_block * NBLK)
     line = None
     if rank == 0:
         cpu_s, cores = cpu_block_seconds(reps=1, threads=os.cpu_count())

@@ -88,9 +88,12 @@ struct SampleScratch {
   __half* P = nullptr;
   __half* ckv = nullptr;  // cross-attention k|v of every block, computed once per sample
   size_t ckv_elems = 0;
+  const __half** modtab = nullptr;  // device: the blocks' AdaLN A weights, then their B weights
+  std::vector<const __half*> modtab_host;
+  float* se = nullptr;              // silu(emb) of the current step
   void release() {
     for (void* p : {(void*)tp, (void*)emb, (void*)tmp, (void*)lora, (void*)h256, (void*)fmod, (void*)y, (void*)P,
-                    (void*)ckv})
+                    (void*)ckv, (void*)modtab, (void*)se})
       cudaFree(p);
     *this = SampleScratch();
   }
@@ -1449,7 +1452,8 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
   const int C = m[HX_A_NCTX];
   const size_t ckv_stride = static_cast<size_t>(B) * C * 2 * D, ckv_need = ckv_stride * nblk;
   SampleScratch& sc = h->ss;
-  if (sc.S < nsteps || sc.D != D || sc.rows < rows || sc.ckv_elems < ckv_need) {
+  if (sc.S < nsteps || sc.D != D || sc.rows < rows || sc.ckv_elems < ckv_need ||
+      sc.modtab_host.size() < 2 * static_cast<size_t>(nblk)) {
     cudaStreamSynchronize(h->stream);
     h->drop_graphs();
     sc.release();
@@ -1458,7 +1462,9 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
               cudaMalloc(&sc.tmp, S * D * 4) == cudaSuccess && cudaMalloc(&sc.lora, S * 3 * D * 4) == cudaSuccess &&
               cudaMalloc(&sc.h256, S * 256 * 4) == cudaSuccess && cudaMalloc(&sc.fmod, S * 2 * D * 4) == cudaSuccess &&
               cudaMalloc(&sc.y, rows * 64 * 4) == cudaSuccess && cudaMalloc(&sc.P, rows * 128 * 2) == cudaSuccess &&
-              cudaMalloc(&sc.ckv, ckv_need * 2) == cudaSuccess;
+              cudaMalloc(&sc.ckv, ckv_need * 2) == cudaSuccess &&
+              cudaMalloc(&sc.modtab, 2 * static_cast<size_t>(nblk) * sizeof(void*)) == cudaSuccess &&
+              cudaMalloc(&sc.se, static_cast<size_t>(D) * 4) == cudaSuccess;
     if (!ok) {
       sc.release();
       return (*rc = HX_E_CUDA);
@@ -1467,6 +1473,20 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
     sc.D = D;
     sc.rows = rows;
     sc.ckv_elems = ckv_need;
+    sc.modtab_host.assign(2 * static_cast<size_t>(nblk), nullptr);
+  }
+  {  // the blocks' AdaLN weights for the batched modulation (uploaded when they change)
+    std::vector<const __half*> tab(sc.modtab_host.size(), nullptr);
+    for (int k = 0; k < nblk; ++k) {
+      tab[k] = ws[k]->modA;
+      tab[nblk + k] = ws[k]->modB;
+    }
+    if (tab != sc.modtab_host) {
+      if (cudaMemcpyAsync(sc.modtab, tab.data(), tab.size() * sizeof(void*), cudaMemcpyHostToDevice, h->stream) !=
+          cudaSuccess)
+        return (*rc = HX_E_CUDA);
+      sc.modtab_host = tab;
+    }
   }
   if (int r = ensure_modscratch(h, kModStride(D) * nblk)) return (*rc = r);
   uint8_t* blob = static_cast<uint8_t*>(bi->second.ptr);
@@ -1492,8 +1512,12 @@ int hx_anima_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const
       ge.x = x;
       ge.ldx = D;
       CKL(gemm_launch(ge, s));
-      if (int r = chain_body(h, ws, m.data(), blob, nullptr, sc.emb + static_cast<size_t>(i) * D,
-                             sc.lora + static_cast<size_t>(i) * 3 * D, 0, 0, sc.ckv, ckv_stride))
+      // the 36 blocks' modulation vectors of this step in one pair of launches
+      const size_t per = kModStride(D);
+      CKL(modulation_batch_launch(sc.modtab, sc.modtab + nblk, nblk, sc.emb + static_cast<size_t>(i) * D,
+                                  sc.lora + static_cast<size_t>(i) * 3 * D, h->modscratch, per, sc.se, 3, D, 256,
+                                  3 * D, s));
+      if (int r = chain_body(h, ws, m.data(), blob, h->modscratch, nullptr, nullptr, 0, per, sc.ckv, ckv_stride))
         return r;
       const float* fm = sc.fmod + static_cast<size_t>(i) * 2 * D;
       CKL(lnmod_launch(x, hbuf, static_cast<int>(rows), D, fm, fm + D, 0, T, 1e-6f, s));

@@ -146,6 +146,57 @@ __global__ void mod_stage2(const __half* __restrict__ Bw, const float* __restric
   if (lane == 0) out[gw] = acc + (lora ? lora[o] : 0.f);
 }
 
+// The same two stages for every block of a chain at once (blockIdx.y = block), weights from per-block
+// pointer tables, silu(emb) computed once (silu_kernel) instead of in every warp; out for block b at
+// out + b * out_stride: [nsite][O] outputs, then [nsite][R] hidden.
+__global__ void silu_kernel(const float* __restrict__ e, float* __restrict__ y, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = e[i] / (1.f + expf(-e[i]));
+}
+__global__ void mod_batch_stage1(const __half* const* __restrict__ Atab, const float* __restrict__ se,
+                                 float* __restrict__ out, size_t out_stride, int nsite, int D, int R, int O) {
+  const int lane = threadIdx.x & 31, b = blockIdx.y;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= nsite * R) return;
+  const __half* row = Atab[b] + static_cast<size_t>(gw) * D;
+  float acc = 0.f;
+  for (int i = lane * 8; i < D; i += 256) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(row + i);
+    const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 wf = __half22float2(w2[t]);
+      acc = fmaf(wf.x, se[i + 2 * t], acc);
+      acc = fmaf(wf.y, se[i + 2 * t + 1], acc);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) out[b * out_stride + static_cast<size_t>(nsite) * O + gw] = acc;
+}
+__global__ void mod_batch_stage2(const __half* const* __restrict__ Btab, const float* __restrict__ lora,
+                                 float* __restrict__ out, size_t out_stride, int nsite, int R, int O) {
+  const int lane = threadIdx.x & 31, b = blockIdx.y;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gw >= nsite * O) return;
+  const int site = gw / O, o = gw % O;
+  float* ob = out + b * out_stride;
+  const __half* row = Btab[b] + static_cast<size_t>(gw) * R;
+  const float* hs = ob + static_cast<size_t>(nsite) * O + static_cast<size_t>(site) * R;
+  float acc = 0.f;
+  for (int j = lane * 8; j < R; j += 256) {
+    const uint4 wv = *reinterpret_cast<const uint4*>(row + j);
+    const __half2* w2 = reinterpret_cast<const __half2*>(&wv);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float2 wf = __half22float2(w2[t]);
+      acc = fmaf(wf.x, hs[j + 2 * t], acc);
+      acc = fmaf(wf.y, hs[j + 2 * t + 1], acc);
+    }
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) ob[gw] = acc + (lora ? lora[o] : 0.f);
+}
+
 __global__ void f32_to_f16_kernel(const float* __restrict__ s, __half* __restrict__ d, size_t n) {
   const size_t i = (static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
   if (i + 3 < n) {
@@ -167,6 +218,19 @@ cudaError_t rmsmod_launch(const float* x, __half* h, int rows, int D, const floa
                           const float* scale, long vec_bstride, int rows_per_img, float eps, cudaStream_t s) {
   if (!w) return cudaErrorInvalidValue;
   return norm_dispatch<true>(x, h, rows, D, w, shift, scale, vec_bstride, rows_per_img, eps, s);
+}
+
+// every block of a chain: Atab / Btab device tables of nblk weight pointers, se a device scratch of D floats
+cudaError_t modulation_batch_launch(const __half* const* Atab, const __half* const* Btab, int nblk, const float* emb,
+                                    const float* lora, float* out, size_t out_stride, float* se, int nsite, int D,
+                                    int R, int O, cudaStream_t s) {
+  if (D % 256 || R % 256 || nblk < 1 || nblk > 65535 || out_stride < static_cast<size_t>(nsite) * (O + R))
+    return cudaErrorInvalidValue;
+  const int t = 256, wpb = t / 32;
+  silu_kernel<<<(D + 255) / 256, 256, 0, s>>>(emb, se, D);
+  mod_batch_stage1<<<dim3((nsite * R + wpb - 1) / wpb, nblk), t, 0, s>>>(Atab, se, out, out_stride, nsite, D, R, O);
+  mod_batch_stage2<<<dim3((nsite * O + wpb - 1) / wpb, nblk), t, 0, s>>>(Btab, lora, out, out_stride, nsite, R, O);
+  return cudaGetLastError();
 }
 
 // hid scratch lives right after the nsite*O outputs: out must hold nsite*(O+R) floats

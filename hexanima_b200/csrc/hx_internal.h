@@ -91,6 +91,9 @@ cudaError_t lnmod_launch(const float* x, __half* h, int rows, int D, const float
                          long vec_bstride, int rows_per_img, float eps, cudaStream_t s);
 cudaError_t rmsmod_launch(const float* x, __half* h, int rows, int D, const float* w, const float* shift,
                           const float* scale, long vec_bstride, int rows_per_img, float eps, cudaStream_t s);
+cudaError_t modulation_batch_launch(const __half* const* Atab, const __half* const* Btab, int nblk, const float* emb,
+                                    const float* lora, float* out, size_t out_stride, float* se, int nsite, int D,
+                                    int R, int O, cudaStream_t s);
 cudaError_t modulation_launch(const __half* Aw, const __half* Bw, const float* emb, const float* lora, float* out,
                               int nsite, int D, int R, int O, cudaStream_t s);
 cudaError_t f32_to_f16_launch(const float* src, __half* dst, size_t n, cudaStream_t s);
