@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "hx_internal.h"
+#include "hx_gelu.cuh"
 #include "hx_ptx.cuh"
 
 namespace hx {
@@ -166,7 +167,6 @@ __device__ __forceinline__ void store_row32_f16(__half* dst, const float* v) {
                       pack_half2(v[8 * q + 4], v[8 * q + 5]), pack_half2(v[8 * q + 6], v[8 * q + 7]));
 }
 
-__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
 __device__ __forceinline__ float situ(float h, float g) {
   return (4.0f * tanhf(g * 0.25f) * (1.0f / (1.0f + expf(-g)))) * (25.0f * tanhf(h * 0.04f));
 }
@@ -213,8 +213,7 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
         if constexpr (EPI == EPI_GELU) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+          gelu32(v);
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q)

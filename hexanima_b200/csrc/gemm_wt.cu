@@ -28,6 +28,7 @@
 #include <cudaTypedefs.h>
 
 #include "hx_internal.h"
+#include "hx_gelu.cuh"
 #include "hx_ptx.cuh"
 
 namespace hx {
@@ -97,7 +98,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* s
   return __all_sync(0xffffffffu, mbar_wait(bar, parity, status, code));
 }
 
-__device__ __forceinline__ float gelu_erf(float v) { return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f)); }
 
 // Column sums of a 32 x 32 block held one row per lane: returns, in lane l, the sum over the 32 lanes
 // of x[l] (five butterfly steps, each halving the columns a lane carries).
@@ -182,8 +182,7 @@ __device__ __forceinline__ void epi_chunk(const WtParams& p, const CUtensorMap* 
       bulk_commit();
     }
   } else if constexpr (EPI == EPI_GELU) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+    gelu32(v);
     store_box_f16<true>(tmO, box, v, lane, e.col0, tok0);  // the mlp hidden stream is larger than L2
   } else if constexpr (EPI == EPI_STORE) {
     store_box_f16<false>(tmO, box, v, lane, e.col0, tok0);

@@ -77,6 +77,30 @@ def test_gemm_store_and_gelu(h, fmt, tile):
         assert rel(out.float(), f(ref)) < 2e-3
 
 
+@pytest.mark.parametrize("tile", TILES)
+def test_gelu_epilogue_ulps(h, tile):
+    """The GELU epilogue's polynomial erfc (csrc/hx_gelu.cuh) on exactly known inputs: a one-hot GEMM
+    passes fp16 weights spanning [-10, 10] through unchanged, so out = fp16(gelu(w)); against the exact
+    erf GELU rounded to fp16: at most one ulp apart, and on at most 2 % of the values."""
+    import scipy.special as sp
+    K, N = 256, 512
+    rng = np.random.default_rng(11)
+    w = np.concatenate((np.linspace(-10, 10, N * K // 2), rng.uniform(-6, 6, N * K // 2))).astype(np.float16)
+    rng.shuffle(w)
+    w = w.reshape(N, K)
+    mat, keep, _ = make_mat(rt.FMT_F16, w.astype(np.float32))
+    A = torch.eye(K, dtype=torch.float16, device="cuda")
+    out = torch.zeros(K, N, dtype=torch.float16, device="cuda")
+    h.gemm(A, K, mat, rt.EPI_GELU, lda=K, out=out, ldo=N, tile=tile)
+    h.sync()
+    got = out.cpu().numpy().T.copy()
+    x = w.astype(np.float64)
+    ref = (0.5 * x * (1 + sp.erf(x / np.sqrt(2)))).astype(np.float16)
+    d = np.abs(got.view(np.int16).astype(np.int32) - ref.view(np.int16).astype(np.int32))
+    d = np.where((got == 0) & (ref == 0), 0, d)  # +0 / -0
+    assert d.max() <= 1 and (d > 0).mean() <= 0.02, (int(d.max()), float((d > 0).mean()))
+
+
 @pytest.mark.parametrize("tile", TILES3)
 def test_gemm_large_k_and_lora_a2(h, tile):
     torch.manual_seed(2)
