@@ -52,7 +52,7 @@ struct KParams {
   int M, N, nkb, nkb1, group;
   int num_m_tiles, num_tiles;
   int num_n_tiles, n_fastest;  // tile order: n_fastest walks the N tiles of one M block consecutively
-  int ksplit;                  // split-K (residual epilogue only): work unit t covers K slice t / (M x N tiles)
+  int streamk;                 // CTA-pair kernel, residual epilogue: stream-K schedule (Sched)
   __half* out;
   int ldo;
   float* x;
@@ -69,21 +69,47 @@ struct KParams {
   int* status;
 };
 
-// work unit t -> (M tile, N tile) in the launch's order, and its K-block range [kb0, kb1): with split-K
-// the units of K slice j are t in [j, j + 1) x (M tiles x N tiles), each reduce-adding a partial sum
+// tile t -> (M tile, N tile) in the launch's order
 __device__ __forceinline__ int tile_m(const KParams& p, int t) {
-  t %= p.num_m_tiles * p.num_n_tiles;
   return p.n_fastest ? t / p.num_n_tiles : t % p.num_m_tiles;
 }
 __device__ __forceinline__ int tile_n(const KParams& p, int t) {
-  t %= p.num_m_tiles * p.num_n_tiles;
   return p.n_fastest ? t % p.num_n_tiles : t / p.num_m_tiles;
 }
-__device__ __forceinline__ void kb_range(const KParams& p, int t, int& kb0, int& kb1) {
-  const int per = (p.nkb + p.ksplit - 1) / p.ksplit;
-  kb0 = (t / (p.num_m_tiles * p.num_n_tiles)) * per;
-  kb1 = min(p.nkb, kb0 + per);
-}
+
+// The work units of CTA pair `pair` in order. Tile schedule: tiles pair, pair + npairs, ..., each over
+// all k-blocks. Stream-K (residual epilogue): the whole waves of tiles keep that order (which keeps the
+// operand blocks the concurrent pairs share in L2); the tiles of the last, partial wave are cut into an
+// equal share of (tile, k-block) iterations per pair, taken tile after tile; a tile cut between two pairs
+// gets two partial sums, each reduce-added into x. Every role of the pair walks the same units.
+struct Sched {
+  int nkb, t, step, full, it, it1;
+  __device__ __forceinline__ Sched(const KParams& p, int pair, int npairs)
+      : nkb(p.nkb), t(pair), step(npairs), full(p.num_tiles), it(0), it1(0) {
+    if (p.streamk) {
+      full = p.num_tiles / npairs * npairs;
+      const long long rem = static_cast<long long>(p.num_tiles - full) * p.nkb, base = static_cast<long long>(full) * p.nkb;
+      it = static_cast<int>(base + rem * pair / npairs);
+      it1 = static_cast<int>(base + rem * (pair + 1) / npairs);
+    }
+  }
+  __device__ __forceinline__ bool next(const KParams& p, int& tile, int& kb0, int& kb1) {
+    (void)p;
+    if (t < full) {
+      tile = t;
+      kb0 = 0;
+      kb1 = nkb;
+      t += step;
+      return true;
+    }
+    if (it >= it1) return false;
+    tile = it / nkb;
+    kb0 = it % nkb;
+    kb1 = min(nkb, kb0 + (it1 - it));
+    it += kb1 - kb0;
+    return true;
+  }
+};
 
 // ---------------------------------------------------------------- dequantisers
 // One k-block (64 k) of a 256-row weight tile: raw smem -> fp16 SW128 K-major smem.
@@ -530,9 +556,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
         const int t = blockIdx.x + ti * gridDim.x;
         const int m0 = tile_m(p, t) * BM, n0 = tile_n(p, t) * BN;
-        int kb0, kb1;
-        kb_range(p, t, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&empty[s], ph ^ 1, p.status, 101)) { ok = false; break; }
@@ -563,9 +587,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (!mbar_wait(&tempty[acc], ((ti >> 1) & 1) ^ 1, p.status, 102)) { ok = false; break; }
         tc_fence_after();
         const uint32_t dt = tmem + acc * BN;
-        int kb0, kb1;
-        kb_range(p, blockIdx.x + ti * gridDim.x, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&full[s], ph, p.status, 103)) { ok = false; break; }
@@ -577,7 +599,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             mma_f16_ss(dt, sdesc_sw128(a0 + 32 * k, 16, 1024), sdesc_sw128(b0 + 32 * k, 16, 1024), idesc,
-                       (kb != kb0 || k != 0));
+                       (kb | k) != 0);
           }
           issued = true;
           mma_commit(&empty[s]);
@@ -596,9 +618,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
-        int kb0, kb1;
-        kb_range(p, blockIdx.x + ti * gridDim.x, kb0, kb1);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kb = 0; kb < p.nkb; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&full[s], ph, p.status, 105)) { ok = false; break; }
@@ -726,7 +746,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t tmem = *tmem_base_slot;
 
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int ntiles_mine = p.num_tiles > pair ? (p.num_tiles - 1 - pair) / npairs + 1 : 0;
   const int row0 = static_cast<int>(rank) * HALF;
 
   if (warp == TMA_WARP) {
@@ -736,11 +755,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t raw_tx = C::RAW_B + sc_rows * HALF * 2 * (FMT == WF_Q4A ? 2 : 1);
       int it = 0;
       bool ok = true;
-      for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
-        const int t = pair + ti * npairs;
+      Sched sched(p, pair, npairs);
+      int t, kb0, kb1;
+      while (ok && sched.next(p, t, kb0, kb1)) {
         const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * BN + row0;
-        int kb0, kb1;
-        kb_range(p, t, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -766,13 +784,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       constexpr uint32_t idesc = idesc_f16(2 * HALF, BN, 0, 0);
       int it = 0;
       bool ok = true, issued = false;
-      for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
+      Sched sched(p, pair, npairs);
+      int t, kb0, kb1;
+      for (int ti = 0; ok && sched.next(p, t, kb0, kb1); ++ti) {
         const int acc = ti & 1;
         if (!mbar_wait(&tempty[acc], ((ti >> 1) & 1) ^ 1, p.status, 112)) { ok = false; break; }
         tc_fence_after();
         const uint32_t dt = tmem + acc * BN;
-        int kb0, kb1;
-        kb_range(p, pair + ti * npairs, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -802,9 +820,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int dt = threadIdx.x - DQ_WARP0 * 32;
       int it = 0;
       bool ok = true;
-      for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
-        int kb0, kb1;
-        kb_range(p, pair + ti * npairs, kb0, kb1);
+      Sched sched(p, pair, npairs);
+      int t, kb0, kb1;
+      while (ok && sched.next(p, t, kb0, kb1)) {
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -819,8 +837,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {  // epilogue warps 0..3: this CTA's 128 rows of the pair tile
     bool ok = true;
-    for (int ti = 0; ti < ntiles_mine && ok; ++ti) {
-      const int t = pair + ti * npairs;
+    Sched sched(p, pair, npairs);
+    int t, kb0, kb1;
+    for (int ti = 0; ok && sched.next(p, t, kb0, kb1); ++ti) {
       const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * BN;
       const int acc = ti & 1;
       if (!mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 116)) { ok = false; break; }
@@ -931,7 +950,8 @@ static cudaError_t launch_pair_t(const GemmArgs& a, const KParams& p, const CUte
   }
   int npairs = sm_count() / 2;
   if (a.max_ctas > 0 && a.max_ctas / 2 < npairs) npairs = a.max_ctas / 2 > 0 ? a.max_ctas / 2 : 1;
-  if (p.num_tiles < npairs) npairs = p.num_tiles;
+  const long long units = p.streamk ? static_cast<long long>(p.num_tiles) * p.nkb : p.num_tiles;
+  if (units < npairs) npairs = static_cast<int>(units);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * npairs);
   cfg.blockDim = dim3(GEMM_THREADS);
@@ -1008,25 +1028,22 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   const int single_tiles = ((a.M + BM - 1) / BM) * ((N + BN - 1) / BN);
   bool pair = a.tile == 2 || (a.tile == 0 && (pair_tiles + sm_count() / 2 - 1) / (sm_count() / 2) <=
                                                  (single_tiles + sm_count() - 1) / sm_count());
-  // residual GEMMs with few tiles (one or two images per GPU): split K so that the work units fill the
-  // GPU; each unit reduce-adds its partial product into x (the sum order of the slices is not fixed).
-  // Model: waves x (k-blocks per unit + a fixed cost per unit for pipeline fill and epilogue), CTA pairs
-  // about 15 % faster per k-block than single CTAs; a split must promise at least 8 %.
-  int ksplit = 1;
+  // residual GEMMs with fewer than two waves of pair tiles (one or two images per GPU): the CTA-pair
+  // kernel with a stream-K tail, so no pair idles through a mostly empty last wave (one image: 48 tiles on
+  // 74 pairs; down projection 68 -> 55 us, two images 122 -> 93 us). Tiles cut between two pairs reduce-add two
+  // partial sums into x, in no fixed order. From two waves up the plain tile schedule stays: at 4 and 8
+  // images the GEMMs run at the power cap, where the idle tail costs energy rather than time, and both
+  // schedules measured the same, so x stays bit-reproducible there.
+  // Each pair's share of the tail must be at least 32 k-blocks: shorter units (the o projection, K = 2048,
+  // at one or two images: 21 and 10 k-blocks) lose more to their pipeline fill and extra partial tiles
+  // than the balance gains.
+  int streamk = 0;
   if (a.epi == EPI_RESID && a.tile == 0 && a.max_ctas == 0) {
-    const int nkb = K / BK, nsm = sm_count(), npairs = nsm / 2;
-    constexpr double kUnitCost = 8.0;
-    auto waves = [](long units, long slots) { return static_cast<double>((units + slots - 1) / slots); };
-    double best = (pair ? waves(pair_tiles, npairs) : 1.15 * waves(single_tiles, nsm)) * (nkb + kUnitCost);
-    for (int ks = 2; ks <= 4; ++ks) {
-      const int per = (nkb + ks - 1) / ks;
-      if (per < 8 || (ks - 1) * per >= nkb) break;
-      const double c = waves(static_cast<long>(pair_tiles) * ks, npairs) * (per + kUnitCost);
-      if (c < 0.92 * best) {
-        best = c;
-        ksplit = ks;
-        pair = true;
-      }
+    const int npairs = sm_count() / 2;
+    const long long tail = static_cast<long long>(pair_tiles % npairs) * (K / BK);
+    if (pair_tiles < 2 * npairs && tail >= 32LL * npairs) {
+      pair = true;
+      streamk = 1;
     }
   }
   const uint32_t wrows = pair ? HALF : BN;
@@ -1079,8 +1096,8 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   p.group = W->fmt == WF_F16 ? 64 : W->group;
   p.num_m_tiles = pair ? (a.M + 2 * HALF - 1) / (2 * HALF) : (a.M + BM - 1) / BM;
   p.num_n_tiles = (N + BN - 1) / BN;
-  p.ksplit = ksplit;
-  p.num_tiles = p.num_m_tiles * p.num_n_tiles * ksplit;
+  p.streamk = streamk;
+  p.num_tiles = p.num_m_tiles * p.num_n_tiles;
   // default order walks M tiles under one weight block (the weight block stays in L2); when the A
   // operand is far larger than L2 but the weights fit (the mlp down projection reading the 8-image
   // hidden state), walk the N tiles of one A block instead so A streams from HBM once
