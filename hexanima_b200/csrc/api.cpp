@@ -123,6 +123,8 @@ struct hx_ctx {
   int next_fd = 1;
   float* modscratch = nullptr;  // chain modulation vectors
   size_t modscratch_floats = 0;
+  __half* wexp = nullptr;  // fp16 expansion of one quantised matrix before its GEMM (stream-ordered)
+  size_t wexp_bytes = 0;
   cudaEvent_t ev[34] = {};
   std::vector<ChainGraph> graphs;
   uint64_t graph_clock = 0;
@@ -372,6 +374,8 @@ inline __half* hptr(uint8_t* blob, int off) { return reinterpret_cast<__half*>(b
 
 GemmArgs gargs(hx_ctx* h, const __half* A, int lda, int M, const DevMat* W, int epi) {
   GemmArgs g;
+  g.wexp = h->wexp;
+  g.wexp_bytes = h->wexp_bytes;
   g.A = A;
   g.lda = lda;
   g.M = M;
@@ -380,6 +384,35 @@ GemmArgs gargs(hx_ctx* h, const __half* A, int lda, int M, const DevMat* W, int 
   g.epi = epi;
   g.status = h->status;
   return g;
+}
+
+// Grow the weight-expansion scratch to `bytes` (outside graph capture only; captured graphs hold the old
+// pointer and are dropped). A failed allocation leaves no scratch: the GEMMs then dequantise in-kernel.
+void reserve_wexp(hx_ctx* h, size_t bytes) {
+  if (bytes <= h->wexp_bytes) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(h->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return;
+  cudaStreamSynchronize(h->stream);
+  h->drop_graphs();
+  cudaFree(h->wexp);
+  h->wexp = nullptr;
+  h->wexp_bytes = 0;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  h->wexp = static_cast<__half*>(p);
+  h->wexp_bytes = bytes;
+}
+
+// the scratch a weight set needs: its largest quantised matrix as fp16
+size_t wexp_need(const Weights& W) {
+  size_t need = 0;
+  for (int i = 0; i < HX_NMATS; ++i)
+    if (W.has[i] && W.mats[i].fmt != WF_F16)
+      need = std::max(need, static_cast<size_t>(W.mats[i].N) * W.mats[i].K * 2);
+  return need;
 }
 
 // cross-attention k|v of one Anima block: [rows][2D] fp16, k RMS-normalised with the ck gain
@@ -822,6 +855,7 @@ int hx_close(hx_handle hh) {
     for (auto& kv : h->weights)
       for (void* p : kv.second->owned) cudaFree(p);
     cudaFree(h->modscratch);
+    cudaFree(h->wexp);
     for (auto& kv : h->glues)
       for (void* p : kv.second->owned) cudaFree(p);
     for (auto& kv : h->moss_glues)
@@ -955,6 +989,7 @@ int hx_weights_load(hx_handle hh, int model, const void* pack, size_t bytes, int
     for (void* p : W->owned) cudaFree(p);
     return rc;
   }
+  reserve_wexp(h, wexp_need(*W));
   *wfd = h->next_fd++;
   h->weights[*wfd] = std::move(W);
   return HX_OK;
@@ -983,6 +1018,8 @@ int hx_weights_bind(hx_handle hh, const hx_weight_desc* d, int* wfd) {
     W->mats[HX_W_O] = to_devmat(d->mats[HX_W_O]);
     W->has[HX_W_O] = true;
     std::lock_guard<std::mutex> lk(h->mu);
+    DevGuard g(h->device);
+    reserve_wexp(h, wexp_need(*W));
     *wfd = h->next_fd++;
     h->weights[*wfd] = std::move(W);
     return HX_OK;
@@ -1004,6 +1041,8 @@ int hx_weights_bind(hx_handle hh, const hx_weight_desc* d, int* wfd) {
     W->has[slot] = true;
   }
   std::lock_guard<std::mutex> lk(h->mu);
+  DevGuard g(h->device);
+  reserve_wexp(h, wexp_need(*W));
   *wfd = h->next_fd++;
   h->weights[*wfd] = std::move(W);
   return HX_OK;
@@ -1872,6 +1911,10 @@ int hx_gemm(hx_handle hh, const hx_gemm_desc* d) {
   a.eps = d->eps > 0.f ? d->eps : 1e-6f;
   a.tile = d->tile;
   a.status = h->status;
+  if (W.fmt != WF_F16 && (a.tile == 4 || (a.tile == 0 && a.M >= expand_min_rows())))
+    reserve_wexp(h, static_cast<size_t>(W.N) * W.K * 2);
+  a.wexp = h->wexp;
+  a.wexp_bytes = h->wexp_bytes;
   cudaError_t e = gemm_launch(a, h->stream);
   return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);
 }

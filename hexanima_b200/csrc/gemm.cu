@@ -22,6 +22,7 @@
 // tile i+1.
 #include <cudaTypedefs.h>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "hx_internal.h"
@@ -906,6 +907,14 @@ bool make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void*
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int expand_min_rows() {
+  static const int rows = [] {
+    const char* e = getenv("HX_EXPAND_ROWS");
+    return e && *e ? atoi(e) : 3072;
+  }();
+  return rows;
+}
+
 int sm_count() {
   static int n[64] = {0};
   int dev = 0;
@@ -1013,6 +1022,32 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   if (W->fmt == WF_Q8 && W->group != 32 && W->group != 64) return cudaErrorInvalidValue;
   if ((W->fmt == WF_Q4 || W->fmt == WF_Q4A) && W->group != 32) return cudaErrorInvalidValue;
+
+  // Quantised weights with enough rows to amortise it: expand W to fp16 in the caller's scratch (one
+  // memory-bound pass, 3 bytes per q8 weight), then run the fp16 kernels, which move no raw tile or
+  // scales through shared memory and need no dequant warps in the main loop. On the 8-image Anima block
+  // the q8 GEMMs run 12-21 % faster this way; the pass costs about N K 3 bytes of HBM / L2 traffic, so
+  // it pays from about two images (3072 rows) up.
+  if (W->fmt != WF_F16 && a.tile != 3 && (a.tile == 4 || (a.tile == 0 && a.M >= expand_min_rows()))) {
+    const size_t need = static_cast<size_t>(N) * K * 2;
+    if (a.wexp && a.wexp_bytes >= need) {
+      cudaError_t e = expand_launch(*W, a.wexp, s);
+      if (e != cudaSuccess) return e;
+      DevMat f;
+      f.fmt = WF_F16;
+      f.N = N;
+      f.K = K;
+      f.group = 64;
+      f.w = a.wexp;
+      GemmArgs b = a;
+      b.W = &f;
+      b.tile = 0;
+      b.wexp = nullptr;
+      b.wexp_bytes = 0;
+      return gemm_launch(b, s);
+    }
+    if (a.tile == 4) return cudaErrorInvalidValue;  // forced, but no scratch of N K fp16
+  }
 
   // q8 weights: the kernel that keeps the dequantised weights in TMEM takes the RMS (q/k/v projection)
   // epilogue when its tiles fill the GPU; measured on the 8-image block shapes it is 2-3 % faster there

@@ -58,7 +58,12 @@ struct GemmArgs {
   float eps = 1e-6f;
   int* status = nullptr;
   int max_ctas = 0;  // 0 = one CTA per SM
-  int tile = 0;      // 0 auto, 1 single-CTA 128x256 tiles, 2 CTA-pair 256x256 tiles, 3 weights in TMEM
+  // 0 auto, 1 single-CTA 128x256 tiles, 2 CTA-pair 256x256 tiles, 3 q8 weights in TMEM, 4 quantised
+  // weights expanded to fp16 in wexp first (auto does so from expand_min_rows() rows up)
+  int tile = 0;
+  // scratch for the expanded weights (fp16 [N][K]); nullptr or too small: dequantise inside the GEMM
+  __half* wexp = nullptr;
+  size_t wexp_bytes = 0;
 };
 
 struct AttnArgs {
@@ -85,6 +90,11 @@ bool gemm_wt_eligible(const GemmArgs& a);
 int gemm_wt_tiles(const GemmArgs& a);
 cudaError_t gemm_wt_launch(const GemmArgs& a, cudaStream_t s);
 cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s);
+// quantised W -> fp16 [N][K] at dst (expand.cu), bit-identical to the GEMMs' own dequantisers
+cudaError_t expand_launch(const DevMat& W, __half* dst, cudaStream_t s);
+// GEMMs with at least this many rows expand quantised weights first when a scratch is given
+// (default 3072 = two 1536-token images; environment HX_EXPAND_ROWS overrides, read once)
+int expand_min_rows();
 
 // memory-bound kernels (elem.cu)
 cudaError_t lnmod_launch(const float* x, __half* h, int rows, int D, const float* shift, const float* scale,

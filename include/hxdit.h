@@ -375,7 +375,9 @@ typedef struct {
   int seg1, seg2, rope0, rope1;
   const float* cos_t; const float* sin_t;   /* [rows_per_img][64] */
   float eps;
-  int tile;                     /* 0 auto, 1 single-CTA 128x256, 2 CTA-pair 256x256, 3 q8 weights in TMEM */
+  int tile;                     /* 0 auto, 1 single-CTA 128x256, 2 CTA-pair 256x256, 3 q8 weights in TMEM,
+                                   4 quantised weights expanded to fp16 in the handle's scratch first (auto
+                                   does so from 3072 rows up; HX_EXPAND_ROWS in the environment overrides) */
 } hx_gemm_desc;
 #define HX_EPI_STORE 0
 #define HX_EPI_RESID 1

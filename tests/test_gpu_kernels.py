@@ -25,7 +25,7 @@ def h():
 
 
 TILES = [1, 2]  # single-CTA 128x256 tiles, CTA-pair 256x256 tiles (cta_group::2)
-TILES3 = [1, 2, 3]  # + q8 weights dequantised into TMEM (256 weight rows x 192 tokens per CTA pair)
+TILES3 = [1, 2, 3, 4]  # + q8 weights dequantised into TMEM; quantised weights expanded to fp16 first
 
 
 def _onehot_dequant(h, fmt, w, group, tile):
@@ -174,7 +174,7 @@ def test_gemm_rms_rope_segments(h, tile):
     torch.manual_seed(4)
     T, K, D = 192, 256, 256  # 2 heads per segment; q | k | v = 768 columns
     A = torch.randn(T, K).half()
-    fmt = rt.FMT_Q8 if tile == 3 else rt.FMT_F16
+    fmt = rt.FMT_Q8 if tile in (3, 4) else rt.FMT_F16
     mat, keep, Wd = make_mat(fmt, (torch.randn(3 * D, K) * 0.05).numpy(), 64)
     gq, gk = 1 + 0.1 * torch.randn(128), 1 + 0.1 * torch.randn(128)
     ang = torch.rand(T, 64) * 6.0
@@ -192,7 +192,7 @@ def test_gemm_rms_rope_segments(h, tile):
     assert rel(o[:, :D], q) < 2e-3 and rel(o[:, D:2 * D], k) < 2e-3 and rel(o[:, 2 * D:], ref[:, 2 * D:]) < 2e-3
 
 
-@pytest.mark.parametrize("tile", TILES)
+@pytest.mark.parametrize("tile", [1, 2, 4])
 def test_gemm_situ(h, tile):
     torch.manual_seed(5)
     M, K, F = 200, 256, 512
@@ -207,6 +207,28 @@ def test_gemm_situ(h, tile):
     ug = _ref_gemm(A, Wd).view(M, F // 128, 2, 128)
     ref = om.situ(ug[:, :, 0], ug[:, :, 1]).reshape(M, F)
     assert rel(out.float(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("fmt,group", [(rt.FMT_Q8, 64), (rt.FMT_Q8, 32), (rt.FMT_Q4, 32), (rt.FMT_Q4A, 32)])
+def test_expanded_weights_same_bits(h, fmt, group):
+    """From 3072 rows up the automatic choice expands quantised weights to fp16 in the handle's scratch and
+    runs the fp16 kernel: the same operand values and k order as the CTA-pair kernel's own dequantisers,
+    so the outputs agree bit for bit (store epilogue, with LoRA extra K columns)."""
+    torch.manual_seed(12)
+    M, K1, N = 3072, 1024, 512
+    A = (torch.randn(M, K1, device="cuda") * 0.5).half()
+    L = torch.randn(M, 128, device="cuda").half()
+    mat, keep, Wd = make_mat(fmt, (torch.randn(N, K1 + 128) * 0.05).numpy(), group)
+    outs = []
+    for tile in (2, 0, 4):
+        o = torch.zeros(M, N, dtype=torch.float16, device="cuda")
+        h.gemm(A, M, mat, rt.EPI_STORE, lda=K1, k1=K1, a2=L.data_ptr(), lda2=128, out=o, ldo=N, tile=tile)
+        outs.append(o)
+    h.sync()
+    ref = torch.cat((A.float().cpu(), L.float().cpu()), 1) @ Wd.T
+    assert rel(outs[0].float().cpu(), ref) < 2e-3
+    for o in outs[1:]:
+        assert torch.equal(o.view(torch.int16), outs[0].view(torch.int16)), int((o != outs[0]).sum())
 
 
 @pytest.mark.parametrize("fmt", [rt.FMT_F16, rt.FMT_Q8, rt.FMT_Q4A])
