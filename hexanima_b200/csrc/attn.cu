@@ -232,6 +232,8 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the previous kernel's outputs (q, k, v) are complete
+  grid_dep_launch();
 
   if (warp == TMA_WARP) {
     if (lane == 0) {
@@ -542,8 +544,9 @@ cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s) {
   p.nqp = (a.Tq + QPAIR - 1) / QPAIR;
   const long nitems = static_cast<long>(p.nqp) * a.H * a.B;
   const int grid = static_cast<int>(nitems < sm_count() ? nitems : sm_count());
-  attn_kernel<<<grid, ATT_THREADS, ATT_SMEM, s>>>(tQ, tK, tV, p, a.q_col0, a.k_col0, a.v_col0);
-  return cudaGetLastError();
+  const cudaError_t e =
+      launch_pdl(attn_kernel, dim3(grid), dim3(ATT_THREADS), ATT_SMEM, s, tQ, tK, tV, p, a.q_col0, a.k_col0, a.v_col0);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace hx

@@ -30,6 +30,8 @@ __global__ void __launch_bounds__(256) norm_mod_kernel(const float* __restrict__
                                                        const float* __restrict__ scale, long vec_bstride,
                                                        int rows_per_img, float eps) {
   constexpr int D = 128 * NV;
+  grid_dep_wait();  // x is complete
+  grid_dep_launch();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -86,9 +88,11 @@ cudaError_t norm_dispatch(const float* x, __half* h, int rows, int D, const floa
   const int threads = 256, rpb = threads / 32;
   const int grid = (rows + rpb - 1) / rpb;
   if (rows_per_img <= 0) rows_per_img = 1 << 30;
+  cudaError_t e = cudaSuccess;
 #define HX_NORM_CASE(NV)                                                                                   \
   case 128 * NV:                                                                                            \
-    norm_mod_kernel<NV, RMS><<<grid, threads, 0, s>>>(x, h, rows, w, shift, scale, vec_bstride, rows_per_img, eps); \
+    e = launch_pdl(norm_mod_kernel<NV, RMS>, dim3(grid), dim3(threads), 0, s, x, h, rows, w, shift, scale, vec_bstride, \
+                   rows_per_img, eps);                                                                     \
     break;
   switch (D) {
     HX_NORM_CASE(1) HX_NORM_CASE(2) HX_NORM_CASE(3) HX_NORM_CASE(4) HX_NORM_CASE(6) HX_NORM_CASE(8)
@@ -96,7 +100,7 @@ cudaError_t norm_dispatch(const float* x, __half* h, int rows, int D, const floa
     default: return cudaErrorInvalidValue;
   }
 #undef HX_NORM_CASE
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // ---------------------------------------------------------------- modulation mat-vecs

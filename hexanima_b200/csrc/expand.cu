@@ -72,6 +72,8 @@ template <int FMT>
 __global__ void __launch_bounds__(EXP_THREADS) expand_kernel(const uint8_t* __restrict__ u, const __half* __restrict__ sc,
                                                              const __half* __restrict__ mn, uint32_t N, uint32_t upr,
                                                              uint32_t units, uint32_t gshift, uint4* __restrict__ w) {
+  grid_dep_wait();  // the previous user of the scratch (the GEMM before) has finished reading it
+  grid_dep_launch();
   const uint32_t stride = gridDim.x * EXP_THREADS * UNROLL;
   for (uint32_t base = blockIdx.x * EXP_THREADS * UNROLL + threadIdx.x; base < units; base += stride) {
     uint2 v8[UNROLL];
@@ -116,20 +118,22 @@ cudaError_t expand_launch(const DevMat& W, __half* dst, cudaStream_t s) {
   const auto* u = static_cast<const uint8_t*>(W.w);
   auto* out = reinterpret_cast<uint4*>(dst);
   const uint32_t N = W.N, upr = W.K / 8, nu = static_cast<uint32_t>(units);
+  const __half* no_min = nullptr;
+  cudaError_t e = cudaSuccess;
   switch (W.fmt) {
     case WF_Q8:
-      expand_kernel<WF_Q8><<<grid, EXP_THREADS, 0, s>>>(u, W.scale, nullptr, N, upr, nu, gshift, out);
+      e = launch_pdl(expand_kernel<WF_Q8>, dim3(grid), dim3(EXP_THREADS), 0, s, u, W.scale, no_min, N, upr, nu, gshift, out);
       break;
     case WF_Q4:
-      expand_kernel<WF_Q4><<<grid, EXP_THREADS, 0, s>>>(u, W.scale, nullptr, N, upr, nu, gshift, out);
+      e = launch_pdl(expand_kernel<WF_Q4>, dim3(grid), dim3(EXP_THREADS), 0, s, u, W.scale, no_min, N, upr, nu, gshift, out);
       break;
     case WF_Q4A:
-      expand_kernel<WF_Q4A><<<grid, EXP_THREADS, 0, s>>>(u, W.scale, W.minv, N, upr, nu, gshift, out);
+      e = launch_pdl(expand_kernel<WF_Q4A>, dim3(grid), dim3(EXP_THREADS), 0, s, u, W.scale, W.minv, N, upr, nu, gshift, out);
       break;
     default:
       return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace hx

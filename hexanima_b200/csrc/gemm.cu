@@ -541,6 +541,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_slot;
+  grid_dep_wait();  // the previous kernel's outputs (A, x) are complete
+  grid_dep_launch();
 
   const int ntiles_mine = (p.num_tiles > static_cast<int>(blockIdx.x))
                               ? (p.num_tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
@@ -745,6 +747,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM of the pair allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_base_slot;
+  grid_dep_wait();  // the previous kernel's outputs (A, x) are complete
+  grid_dep_launch();
 
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int row0 = static_cast<int>(rank) * HALF;
@@ -915,6 +919,14 @@ int expand_min_rows() {
   return rows;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("HX_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 int sm_count() {
   static int n[64] = {0};
   int dev = 0;
@@ -940,8 +952,9 @@ static cudaError_t launch_t(const GemmArgs& a, const KParams& p, const CUtensorM
   int grid = sm_count();
   if (a.max_ctas > 0 && a.max_ctas < grid) grid = a.max_ctas;
   if (p.num_tiles < grid) grid = p.num_tiles;
-  gemm_kernel<FMT, EPI><<<grid, GEMM_THREADS, C::SMEM, s>>>(tA, tA2, tW, tS, tMin, tX, p);
-  return cudaGetLastError();
+  const cudaError_t e = launch_pdl(gemm_kernel<FMT, EPI>, dim3(grid), dim3(GEMM_THREADS), C::SMEM, s, tA, tA2, tW, tS,
+                                   tMin, tX, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int FMT, int EPI>
@@ -966,13 +979,13 @@ static cudaError_t launch_pair_t(const GemmArgs& a, const KParams& p, const CUte
   cfg.blockDim = dim3(GEMM_THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_attr(attr, 1);
   return cudaLaunchKernelEx(&cfg, gemm2_kernel<FMT, EPI>, tA, tA2, tW, tS, tMin, tX, p);
 }
 

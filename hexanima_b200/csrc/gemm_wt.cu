@@ -291,6 +291,8 @@ __global__ void __launch_bounds__(WT_THREADS, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM of the pair allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  grid_dep_wait();  // the previous kernel's outputs (the token rows) are complete
+  grid_dep_launch();
 
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int ntiles_mine = p.num_tiles > pair ? (p.num_tiles - 1 - pair) / npairs + 1 : 0;
@@ -487,13 +489,13 @@ cudaError_t launch_wt(const WtParams& p, const CUtensorMap& tA, const CUtensorMa
   cfg.blockDim = dim3(WT_THREADS);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_attr(attr, 1);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_wt_kernel<EPI>, tA, tA2, tW, tS, tO, p);
   if (e != cudaSuccess) cudaGetLastError();  // a refused launch leaves no error for the next caller
   return e;

@@ -155,4 +155,29 @@ cudaError_t lora_fold_slots(const DevMat& W, int k_base, int row_mode, const Dev
                             const float* Au, int rank, float scale, cudaStream_t s);
 int sm_count();
 
+// Kernels of the block chain are launched with programmatic stream serialization: a kernel's launch and
+// prologue (barrier set-up, TMEM allocation, tensor-map prefetch) overlap the tail of the kernel before
+// it, and it waits in grid_dep_wait() (hx_ptx.cuh) before its first global-memory access. Every kernel
+// launched through pdl_attr executes that wait. HX_PDL=0 in the environment turns it off (read once).
+bool pdl_enabled();
+// appends the attribute to attrs when enabled; returns the new attribute count
+inline unsigned pdl_attr(cudaLaunchAttribute* attrs, unsigned n) {
+  if (!pdl_enabled()) return n;
+  attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[n].val.programmaticStreamSerializationAllowed = 1;
+  return n + 1;
+}
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_attr(attr, 0);
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 }  // namespace hx

@@ -29,6 +29,13 @@ __device__ __forceinline__ uint64_t globaltimer() {
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may start
+// before its predecessor in the stream has finished: grid_dep_wait() returns once the predecessor grid
+// has completed and its memory operations are visible (at once when there is none), and must come
+// before the kernel's first global-memory access. grid_dep_launch() lets the next such kernel start.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
