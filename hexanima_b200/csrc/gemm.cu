@@ -1062,17 +1062,31 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
     if (a.tile == 4) return cudaErrorInvalidValue;  // forced, but no scratch of N K fp16
   }
 
-  // q8 weights: the kernel that keeps the dequantised weights in TMEM takes the RMS (q/k/v projection)
-  // epilogue when its tiles fill the GPU; measured on the 8-image block shapes it is 2-3 % faster there
-  // and 3-7 % slower than the CTA-pair kernel with the store, GELU and residual epilogues
-  if (a.tile == 3) return gemm_wt_launch(a, s);
-  if (a.tile == 0 && a.epi == EPI_RMS && gemm_wt_eligible(a) && gemm_wt_tiles(a) >= sm_count() / 2)
-    return gemm_wt_launch(a, s);
-
   // tile configuration: CTA pairs (256x256 per cluster) unless single-CTA 128x256 tiles need fewer waves
   // (a pair moves half the weight tile per SM, so at equal waves it is the faster of the two: at one
   // image the down projection runs 67 us in pairs against 86 us in single CTAs)
   const int pair_tiles = ((a.M + 2 * HALF - 1) / (2 * HALF)) * ((N + BN - 1) / BN);
+  // residual GEMMs with a long K and fewer than two waves of pair tiles take the stream-K schedule below
+  const bool streamk_candidate = a.epi == EPI_RESID && a.max_ctas == 0 && pair_tiles < sm_count() &&
+                                 static_cast<long long>(pair_tiles % (sm_count() / 2)) * (K / BK) >=
+                                     32LL * (sm_count() / 2);
+
+  // q8 weights below the expansion threshold: the kernel that keeps the dequantised weights in TMEM takes
+  // the RMS (q/k/v projection) epilogue when its tiles fill the GPU (2-3 % faster there than the CTA-pair
+  // kernel, which is 3-7 % faster with the store, GELU and residual epilogues at several waves)
+  if (a.tile == 3) return gemm_wt_launch(a, s);
+  if (a.tile == 0 && gemm_wt_eligible(a)) {
+    const int wt_tiles = gemm_wt_tiles(a), npairs = sm_count() / 2;
+    if (a.epi == EPI_RMS && wt_tiles >= npairs) return gemm_wt_launch(a, s);
+    // at most one wave of tiles with a residual or RMS epilogue (the N = 2048 projections at one image):
+    // each pair has a single tile, so its epilogue is not hidden behind another tile's main loop, and the
+    // TMEM-weight kernel's 8 epilogue warps per CTA with double-buffered per-warp boxes drain it faster
+    // than the CTA-pair kernel's 4 warps and single staging buffer (o projection at one image: 22.5
+    // against 25.6 us)
+    if ((a.epi == EPI_RESID || a.epi == EPI_RMS) && wt_tiles <= npairs && a.max_ctas == 0 && !streamk_candidate)
+      return gemm_wt_launch(a, s);
+  }
+
   const int single_tiles = ((a.M + BM - 1) / BM) * ((N + BN - 1) / BN);
   bool pair = a.tile == 2 || (a.tile == 0 && (pair_tiles + sm_count() / 2 - 1) / (sm_count() / 2) <=
                                                  (single_tiles + sm_count() - 1) / sm_count());
@@ -1086,13 +1100,9 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   // at one or two images: 21 and 10 k-blocks) lose more to their pipeline fill and extra partial tiles
   // than the balance gains.
   int streamk = 0;
-  if (a.epi == EPI_RESID && a.tile == 0 && a.max_ctas == 0) {
-    const int npairs = sm_count() / 2;
-    const long long tail = static_cast<long long>(pair_tiles % npairs) * (K / BK);
-    if (pair_tiles < 2 * npairs && tail >= 32LL * npairs) {
-      pair = true;
-      streamk = 1;
-    }
+  if (a.tile == 0 && streamk_candidate) {
+    pair = true;
+    streamk = 1;
   }
   const uint32_t wrows = pair ? HALF : BN;
 
