@@ -18,10 +18,11 @@ namespace hx {
 
 namespace {
 
-// Work unit: 8 consecutive k of one row (8 bytes of q8 or 4 of q4 in, one 16-byte fp16 store out). Unit i
-// covers elements 8i .. 8i + 7 of the row-major matrix, so a warp's 32 units read 256 (q8) or 128 (q4)
-// contiguous bytes and write 512; each thread keeps UNROLL units' loads in flight before converting.
-constexpr int EXP_THREADS = 256, UNROLL = 4;
+// Work unit: 8 consecutive k of one row (8 bytes of q8 or 4 of q4 in, one 16-byte fp16 store out). The grid
+// is 2D: x runs over the units of a row (a warp's 32 units read 256 or 128 contiguous bytes and write 512),
+// y over groups of EXP_ROWS rows, whose loads each thread issues before converting. No division: a
+// thread's k and scale group are fixed, and the scales of consecutive rows are adjacent.
+constexpr int EXP_THREADS = 256, EXP_ROWS = 4;
 
 __device__ __forceinline__ uint4 q8x8(uint2 v, __half s) {
   // bytes as fp16 0x64uu = 1024 + u exactly; minus 1152 = q exactly; one rounded multiply by s
@@ -67,34 +68,36 @@ __device__ __forceinline__ uint4 q4ax8(uint32_t wd, __half s, __half m) {  // fp
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// FMT: WF_Q8, WF_Q4 or WF_Q4A. units = N K / 8 < 2^32; upr = K / 8 units per row.
+// FMT: WF_Q8, WF_Q4 or WF_Q4A; upr = K / 8 units per row; scale group = 1 << gshift
 template <int FMT>
 __global__ void __launch_bounds__(EXP_THREADS) expand_kernel(const uint8_t* __restrict__ u, const __half* __restrict__ sc,
-                                                             const __half* __restrict__ mn, uint32_t N, uint32_t upr,
-                                                             uint32_t units, uint32_t gshift, uint4* __restrict__ w) {
+                                                             const __half* __restrict__ mn, int N, int upr, int gshift,
+                                                             uint4* __restrict__ w) {
   grid_dep_wait();  // the previous user of the scratch (the GEMM before) has finished reading it
   grid_dep_launch();
-  const uint32_t stride = gridDim.x * EXP_THREADS * UNROLL;
-  for (uint32_t base = blockIdx.x * EXP_THREADS * UNROLL + threadIdx.x; base < units; base += stride) {
-    uint2 v8[UNROLL];
-    uint32_t v4[UNROLL];
-    __half s[UNROLL], m[UNROLL];
+  const int j = blockIdx.x * EXP_THREADS + threadIdx.x;  // unit within the row: k = 8 j .. 8 j + 7
+  if (j >= upr) return;
+  const size_t goff = static_cast<size_t>((8 * j) >> gshift) * N;  // this thread's scale row
+  for (int n0 = blockIdx.y * EXP_ROWS; n0 < N; n0 += gridDim.y * EXP_ROWS) {
+    uint2 v8[EXP_ROWS];
+    uint32_t v4[EXP_ROWS];
+    __half s[EXP_ROWS], m[EXP_ROWS];
 #pragma unroll
-    for (int r = 0; r < UNROLL; ++r) {
-      const uint32_t i = base + r * EXP_THREADS;
-      if (i < units) {
-        const uint32_t n = i / upr, k0 = (i - n * upr) * 8;
-        const size_t g = static_cast<size_t>(k0 >> gshift) * N + n;  // scale [K / group][N]
+    for (int r = 0; r < EXP_ROWS; ++r) {
+      const int n = n0 + r;
+      if (n < N) {
+        const size_t i = static_cast<size_t>(n) * upr + j;
         if constexpr (FMT == WF_Q8) v8[r] = __ldg(reinterpret_cast<const uint2*>(u) + i);
         else v4[r] = __ldg(reinterpret_cast<const uint32_t*>(u) + i);
-        s[r] = __ldg(sc + g);
-        if constexpr (FMT == WF_Q4A) m[r] = __ldg(mn + g);
+        s[r] = __ldg(sc + goff + n);
+        if constexpr (FMT == WF_Q4A) m[r] = __ldg(mn + goff + n);
       }
     }
 #pragma unroll
-    for (int r = 0; r < UNROLL; ++r) {
-      const uint32_t i = base + r * EXP_THREADS;
-      if (i < units) {
+    for (int r = 0; r < EXP_ROWS; ++r) {
+      const int n = n0 + r;
+      if (n < N) {
+        const size_t i = static_cast<size_t>(n) * upr + j;
         if constexpr (FMT == WF_Q8) w[i] = q8x8(v8[r], s[r]);
         else if constexpr (FMT == WF_Q4) w[i] = q4x8(v4[r], s[r]);
         else w[i] = q4ax8(v4[r], s[r], m[r]);
@@ -108,27 +111,27 @@ __global__ void __launch_bounds__(EXP_THREADS) expand_kernel(const uint8_t* __re
 cudaError_t expand_launch(const DevMat& W, __half* dst, cudaStream_t s) {
   if (!W.w || !dst || W.N <= 0 || W.K <= 0 || W.K % 32) return cudaErrorInvalidValue;
   if (reinterpret_cast<uintptr_t>(W.w) % 16 || reinterpret_cast<uintptr_t>(dst) % 16) return cudaErrorInvalidValue;
-  const size_t units = static_cast<size_t>(W.N) * (W.K / 8);
-  if (units >= (1ull << 32)) return cudaErrorInvalidValue;
   if (!W.scale || (W.fmt == WF_Q4A && !W.minv)) return cudaErrorInvalidValue;
   if (W.fmt == WF_Q8 ? (W.group != 32 && W.group != 64) : W.group != 32) return cudaErrorInvalidValue;
-  const uint32_t gshift = W.group == 64 ? 6 : 5;
-  const size_t per_block = static_cast<size_t>(EXP_THREADS) * UNROLL;
-  const int grid = static_cast<int>(std::min<size_t>((units + per_block - 1) / per_block, static_cast<size_t>(sm_count()) * 8));
+  const int gshift = W.group == 64 ? 6 : 5;
+  const int upr = W.K / 8;
+  const int gx = (upr + EXP_THREADS - 1) / EXP_THREADS;
+  const int row_groups = (W.N + EXP_ROWS - 1) / EXP_ROWS;
+  const int gy = std::max(1, std::min(row_groups, sm_count() * 8 / gx));
+  const dim3 grid(gx, gy);
   const auto* u = static_cast<const uint8_t*>(W.w);
   auto* out = reinterpret_cast<uint4*>(dst);
-  const uint32_t N = W.N, upr = W.K / 8, nu = static_cast<uint32_t>(units);
   const __half* no_min = nullptr;
   cudaError_t e = cudaSuccess;
   switch (W.fmt) {
     case WF_Q8:
-      e = launch_pdl(expand_kernel<WF_Q8>, dim3(grid), dim3(EXP_THREADS), 0, s, u, W.scale, no_min, N, upr, nu, gshift, out);
+      e = launch_pdl(expand_kernel<WF_Q8>, grid, dim3(EXP_THREADS), 0, s, u, W.scale, no_min, W.N, upr, gshift, out);
       break;
     case WF_Q4:
-      e = launch_pdl(expand_kernel<WF_Q4>, dim3(grid), dim3(EXP_THREADS), 0, s, u, W.scale, no_min, N, upr, nu, gshift, out);
+      e = launch_pdl(expand_kernel<WF_Q4>, grid, dim3(EXP_THREADS), 0, s, u, W.scale, no_min, W.N, upr, gshift, out);
       break;
     case WF_Q4A:
-      e = launch_pdl(expand_kernel<WF_Q4A>, dim3(grid), dim3(EXP_THREADS), 0, s, u, W.scale, W.minv, N, upr, nu, gshift, out);
+      e = launch_pdl(expand_kernel<WF_Q4A>, grid, dim3(EXP_THREADS), 0, s, u, W.scale, W.minv, W.N, upr, gshift, out);
       break;
     default:
       return cudaErrorInvalidValue;
