@@ -125,6 +125,12 @@ struct hx_ctx {
   size_t modscratch_floats = 0;
   __half* wexp = nullptr;  // fp16 expansion of one quantised matrix before its GEMM (stream-ordered)
   size_t wexp_bytes = 0;
+  // expansions issued ahead of their GEMMs (Anima chain): two fp16 buffers used in turn, filled on a side
+  // stream that forks from and joins back into `stream` through the events below
+  __half* xbuf[2] = {nullptr, nullptr};
+  size_t xbuf_bytes = 0;
+  cudaStream_t xstream = nullptr;
+  cudaEvent_t xev_fork = nullptr, xev_read[2] = {nullptr, nullptr}, xev_ready[2] = {nullptr, nullptr};
   cudaEvent_t ev[34] = {};
   std::vector<ChainGraph> graphs;
   uint64_t graph_clock = 0;
@@ -343,6 +349,8 @@ int load_moss_proj(hx_ctx* h, const uint8_t* pack, size_t bytes, Weights& W) {
 }
 
 // ---------------------------------------------------------------- block orchestration
+class Lookahead;
+
 struct Stage {
   hx_ctx* h;
   int ntimes;
@@ -350,6 +358,8 @@ struct Stage {
   int stop;
   bool stopped = false;
   const __half* ckv_pre = nullptr;  // Anima: this block's cross-attention k|v already computed (sampler cache)
+  Lookahead* xa = nullptr;          // Anima chain: weight expansions issued ahead (nullptr: one per block)
+  const Weights* next = nullptr;    // Anima chain: the next block, whose q|k|v expansion the last GEMM issues
   // returns true when the caller must stop (meta STOP reached)
   bool tick() {
     if (ntimes > 0 && ti < 32) cudaEventRecord(h->ev[ti + 1], h->stream);
@@ -406,6 +416,107 @@ void reserve_wexp(hx_ctx* h, size_t bytes) {
   h->wexp_bytes = bytes;
 }
 
+// Grow the two look-ahead expansion buffers to `bytes` each (outside graph capture; drops captured
+// graphs). On failure there are none and the chain expands in line.
+void reserve_xbuf(hx_ctx* h, size_t bytes) {
+  if (bytes <= h->xbuf_bytes || !h->xstream) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(h->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return;
+  cudaStreamSynchronize(h->stream);
+  cudaStreamSynchronize(h->xstream);
+  h->drop_graphs();
+  for (auto& b : h->xbuf) {
+    cudaFree(b);
+    b = nullptr;
+  }
+  h->xbuf_bytes = 0;
+  void* p0 = nullptr;
+  void* p1 = nullptr;
+  if (cudaMalloc(&p0, bytes) != cudaSuccess || cudaMalloc(&p1, bytes) != cudaSuccess) {
+    cudaFree(p0);
+    cudaGetLastError();
+    return;
+  }
+  h->xbuf[0] = static_cast<__half*>(p0);
+  h->xbuf[1] = static_cast<__half*>(p1);
+  h->xbuf_bytes = bytes;
+}
+
+// Quantised weights expanded to fp16 ahead of their GEMMs. The expansion for a GEMM runs on the handle's
+// side stream into one of two buffers used in turn; it is issued as soon as the GEMM before has been
+// enqueued and waits only for the GEMM that last read its buffer (two GEMMs back), so it runs under the
+// kernels in between (the norm, the attention) instead of in front of its own GEMM. The GEMM waits for it
+// through an event. The same policy as the in-line expansion of gemm_launch decides which GEMMs expand.
+class Lookahead {
+ public:
+  explicit Lookahead(hx_ctx* h) : h_(h) {}
+  Lookahead(const Lookahead&) = delete;
+  Lookahead& operator=(const Lookahead&) = delete;
+  ~Lookahead() { finish(); }
+  // issue the expansion of W for a GEMM of M rows (a no-op when it is already issued or does not apply)
+  cudaError_t issue(const DevMat& W, int M) {
+    if (armed_ && src_ == &W) return cudaSuccess;
+    if (armed_) {  // an expansion nobody consumed: join it before reusing the state
+      cudaError_t e = finish();
+      if (e != cudaSuccess) return e;
+    }
+    const size_t need = static_cast<size_t>(W.N) * W.K * 2;
+    if (W.fmt == WF_F16 || M < expand_min_rows() || !h_->xstream || !h_->xbuf[1] || h_->xbuf_bytes < need)
+      return cudaSuccess;
+    cudaError_t e;
+    if (!started_) {  // fork: the side stream follows everything enqueued on the main stream so far
+      if ((e = cudaEventRecord(h_->xev_fork, h_->stream)) != cudaSuccess) return e;
+      if ((e = cudaStreamWaitEvent(h_->xstream, h_->xev_fork, 0)) != cudaSuccess) return e;
+      started_ = true;
+    }
+    const int b = next_;
+    next_ ^= 1;
+    if (read_[b] && (e = cudaStreamWaitEvent(h_->xstream, h_->xev_read[b], 0)) != cudaSuccess) return e;
+    if ((e = expand_launch(W, h_->xbuf[b], h_->xstream)) != cudaSuccess) return e;
+    if ((e = cudaEventRecord(h_->xev_ready[b], h_->xstream)) != cudaSuccess) return e;
+    armed_ = true;
+    src_ = &W;
+    buf_ = b;
+    view_ = DevMat();
+    view_.fmt = WF_F16;
+    view_.N = W.N;
+    view_.K = W.K;
+    view_.group = 64;
+    view_.w = h_->xbuf[b];
+    return cudaSuccess;
+  }
+  // the GEMM g on the main stream, on the expansion issued for g.W if there is one
+  cudaError_t gemm(GemmArgs g) {
+    const bool use = armed_ && src_ == g.W;
+    cudaError_t e;
+    if (use) {
+      if ((e = cudaStreamWaitEvent(h_->stream, h_->xev_ready[buf_], 0)) != cudaSuccess) return e;
+      g.W = &view_;
+    }
+    if ((e = gemm_launch(g, h_->stream)) != cudaSuccess) return e;
+    if (use) {
+      if ((e = cudaEventRecord(h_->xev_read[buf_], h_->stream)) != cudaSuccess) return e;
+      read_[buf_] = true;
+      armed_ = false;
+    }
+    return cudaSuccess;
+  }
+  // join an expansion that no GEMM consumed (the side stream must end joined, e.g. inside a capture)
+  cudaError_t finish() {
+    if (!armed_) return cudaSuccess;
+    armed_ = false;
+    return cudaStreamWaitEvent(h_->stream, h_->xev_ready[buf_], 0);
+  }
+
+ private:
+  hx_ctx* h_;
+  bool started_ = false, armed_ = false;
+  bool read_[2] = {false, false};  // a GEMM reading buffer b was enqueued after the fork
+  int next_ = 0, buf_ = 0;
+  const DevMat* src_ = nullptr;
+  DevMat view_;
+};
+
 // the scratch a weight set needs: its largest quantised matrix as fp16
 size_t wexp_need(const Weights& W) {
   size_t need = 0;
@@ -441,6 +552,9 @@ int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob,
   const float* cosT = fptr(blob, meta[HX_A_COS]);
   const float* sinT = fptr(blob, meta[HX_A_SIN]);
   const float* gain = W.gain;
+  Lookahead local(h);
+  Lookahead& X = st.xa ? *st.xa : local;
+  CKL(X.issue(W.mats[HX_W_QKV], rows));
   for (int site = 0; site < 3; ++site) {
     const float* sh = mod + (site * 3 + 0) * D;
     const float* sc = mod + (site * 3 + 1) * D;
@@ -459,7 +573,8 @@ int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob,
       g.cosT = cosT;
       g.sinT = sinT;
       g.rows_per_img = T;
-      CKL(gemm_launch(g, s));
+      CKL(X.gemm(g));
+      CKL(X.issue(W.mats[HX_W_O], rows));
       if (st.tick()) return HX_OK;
       if (st.tick()) return HX_OK;  // rope slot: fused into the QKV epilogue
       AttnArgs a;
@@ -475,7 +590,8 @@ int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob,
       go.x = x;
       go.ldx = D;
       go.gate = gt;
-      CKL(gemm_launch(go, s));
+      CKL(X.gemm(go));
+      CKL(X.issue(W.mats[HX_W_CQ], rows));
       if (st.tick()) return HX_OK;
     } else if (site == 1) {
       GemmArgs gq = gargs(h, hbuf, D, rows, &W.mats[HX_W_CQ], EPI_RMS);
@@ -483,7 +599,8 @@ int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob,
       gq.ldo = 3 * D;
       gq.gain0 = gain + 256;
       gq.seg1 = gq.seg2 = D;
-      CKL(gemm_launch(gq, s));
+      CKL(X.gemm(gq));
+      CKL(X.issue(W.mats[HX_W_CO], rows));
       if (st.ckv_pre) {
         ckv = const_cast<__half*>(st.ckv_pre);
       } else {
@@ -504,19 +621,22 @@ int anima_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob,
       go.x = x;
       go.ldx = D;
       go.gate = gt;
-      CKL(gemm_launch(go, s));
+      CKL(X.gemm(go));
+      CKL(X.issue(W.mats[HX_W_M1], rows));
       if (st.tick()) return HX_OK;
     } else {
       GemmArgs g1 = gargs(h, hbuf, D, rows, &W.mats[HX_W_M1], EPI_GELU);
       g1.out = mid;
       g1.ldo = F;
-      CKL(gemm_launch(g1, s));
+      CKL(X.gemm(g1));
+      CKL(X.issue(W.mats[HX_W_M2], rows));
       if (st.tick()) return HX_OK;
       GemmArgs g2 = gargs(h, mid, F, rows, &W.mats[HX_W_M2], EPI_RESID);
       g2.x = x;
       g2.ldx = D;
       g2.gate = gt;
-      CKL(gemm_launch(g2, s));
+      CKL(X.gemm(g2));
+      if (st.next) CKL(X.issue(st.next->mats[HX_W_QKV], rows));
       if (st.tick()) return HX_OK;
     }
   }
@@ -744,6 +864,7 @@ int chain_body(hx_ctx* h, const std::vector<const Weights*>& ws, const int32_t* 
                const __half* ckv_cache = nullptr, size_t ckv_stride = 0) {
   const int model = ws[0]->model, D = ws[0]->D;
   const size_t per = model == HX_MODEL_ANIMA ? kModStride(D) : 6ull * D;
+  Lookahead xa(h);  // Anima: each block's last GEMM issues the next block's q|k|v expansion
   for (size_t k = 0; k < ws.size(); ++k) {
     if ((skipmask >> k) & 1) continue;
     const float* md;
@@ -758,9 +879,17 @@ int chain_body(hx_ctx* h, const std::vector<const Weights*>& ws, const int32_t* 
     }
     Stage st{h, 0, 0, 0};
     if (ckv_cache) st.ckv_pre = ckv_cache + k * ckv_stride;
+    if (model == HX_MODEL_ANIMA) {
+      st.xa = &xa;
+      for (size_t k2 = k + 1; k2 < ws.size(); ++k2)
+        if (!((skipmask >> k2) & 1)) {
+          st.next = ws[k2];
+          break;
+        }
+    }
     if (int r = run_block(h, *ws[k], m, blob, md, st)) return r;
   }
-  return HX_OK;
+  return xa.finish() == cudaSuccess ? HX_OK : HX_E_CUDA;
 }
 
 int ensure_modscratch(hx_ctx* h, size_t floats) {
@@ -839,6 +968,16 @@ int hx_open(int device, hx_handle* out) {
     return HX_E_CUDA;
   }
   for (auto& e : h->ev) cudaEventCreate(&e);
+  // side stream and events of the look-ahead weight expansion (without them the chain expands in line)
+  if (cudaStreamCreateWithFlags(&h->xstream, cudaStreamNonBlocking) != cudaSuccess) {
+    h->xstream = nullptr;
+    cudaGetLastError();
+  }
+  cudaEventCreateWithFlags(&h->xev_fork, cudaEventDisableTiming);
+  for (int b = 0; b < 2; ++b) {
+    cudaEventCreateWithFlags(&h->xev_read[b], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&h->xev_ready[b], cudaEventDisableTiming);
+  }
   *out = reinterpret_cast<hx_handle>(h);
   return HX_OK;
 }
@@ -856,6 +995,14 @@ int hx_close(hx_handle hh) {
       for (void* p : kv.second->owned) cudaFree(p);
     cudaFree(h->modscratch);
     cudaFree(h->wexp);
+    if (h->xstream) cudaStreamSynchronize(h->xstream);
+    for (auto b : h->xbuf) cudaFree(b);
+    if (h->xstream) cudaStreamDestroy(h->xstream);
+    cudaEventDestroy(h->xev_fork);
+    for (int b = 0; b < 2; ++b) {
+      cudaEventDestroy(h->xev_read[b]);
+      cudaEventDestroy(h->xev_ready[b]);
+    }
     for (auto& kv : h->glues)
       for (void* p : kv.second->owned) cudaFree(p);
     for (auto& kv : h->moss_glues)
@@ -990,6 +1137,7 @@ int hx_weights_load(hx_handle hh, int model, const void* pack, size_t bytes, int
     return rc;
   }
   reserve_wexp(h, wexp_need(*W));
+  reserve_xbuf(h, wexp_need(*W));
   *wfd = h->next_fd++;
   h->weights[*wfd] = std::move(W);
   return HX_OK;
@@ -1020,6 +1168,7 @@ int hx_weights_bind(hx_handle hh, const hx_weight_desc* d, int* wfd) {
     std::lock_guard<std::mutex> lk(h->mu);
     DevGuard g(h->device);
     reserve_wexp(h, wexp_need(*W));
+    reserve_xbuf(h, wexp_need(*W));
     *wfd = h->next_fd++;
     h->weights[*wfd] = std::move(W);
     return HX_OK;
@@ -1043,6 +1192,7 @@ int hx_weights_bind(hx_handle hh, const hx_weight_desc* d, int* wfd) {
   std::lock_guard<std::mutex> lk(h->mu);
   DevGuard g(h->device);
   reserve_wexp(h, wexp_need(*W));
+  reserve_xbuf(h, wexp_need(*W));
   *wfd = h->next_fd++;
   h->weights[*wfd] = std::move(W);
   return HX_OK;

@@ -129,6 +129,50 @@ def test_anima_chain_graph_matches_sequential_and_modulation(h):
         h.weights_free(w)
 
 
+def test_anima_chain_weights_expanded_ahead(h):
+    """Two 1536-token images (3072 rows): the chain expands each q8 matrix to fp16 on a side stream ahead of
+    its GEMM (two buffers in turn, the last GEMM of a block issuing the next block's q|k|v). Graph replay,
+    eager per-block calls and the oracle agree."""
+    D, F, Cd, B, T, C, n = 256, 512, 128, 2, 1536, 64, 3
+    sets = [oa.init_weights(70 + i, D=D, F=F, Cd=Cd) for i in range(n)]
+    bound = [anima_bind(h, *s, fmt=rt.FMT_Q8, group=64) for s in sets]
+    wfds = [b[0] for b in bound]
+    x, ctx, _, cos, sin = _anima_inputs(B, T, C, D, Cd, 32, 48, seed=7)
+    emb = torch.randn(D)
+    lora = torch.randn(3 * D) * 0.1
+    meta, total = rt.blob_layout(rt.MODEL_ANIMA, T, C, B, D, F, Cd)
+    A = rt.A
+    bfd = h.buf_alloc(total)
+
+    def load():
+        write_f32(h, bfd, meta[A["X"]], x.numpy())
+        h.buf_write(bfd, meta[A["CTX"]], ctx.half().numpy())
+        write_f32(h, bfd, meta[A["COS"]], cos.numpy())
+        write_f32(h, bfd, meta[A["SIN"]], sin.numpy())
+
+    e, l = emb.cuda(), lora.cuda()
+    ys = []
+    for _ in range(2):  # capture, then replay
+        load()
+        h.chain(meta, wfds, bfd, emb_dev=e, lora_dev=l, use_graph=True)
+        ys.append(read_f32(h, bfd, meta[A["X"]], B * T * D))
+    assert np.array_equal(ys[0], ys[1])
+    load()
+    for i, w in enumerate(wfds):
+        h.mega_block(meta, w, bfd, mod=oa.modulation(sets[i][2], sets[i][3], emb, lora).numpy())
+    y_seq = read_f32(h, bfd, meta[A["X"]], B * T * D)
+    assert rel(torch.from_numpy(ys[0]), torch.from_numpy(y_seq)) < 1e-5
+    xr = x.clone()
+    for i in range(n):
+        Wd, gain = bound[i][1], bound[i][2]
+        xr = oa.block(xr, ctx, oa.modulation(sets[i][2], sets[i][3], emb, lora), cos, sin, Wd, gain)
+    assert rel(torch.from_numpy(ys[0]).view(B, T, D) - x, xr - x) < TOL
+    h.buf_free(bfd)
+    for w in wfds:
+        h.weights_free(w)
+    assert h.status() == 0
+
+
 def _moss_run(h, wfd, x, mod, cos, sin, D, F, nvalid):
     B, T, _ = x.shape
     meta, total = rt.blob_layout(rt.MODEL_MOSS, T, 0, B, D, F)
