@@ -271,6 +271,8 @@ void* g_noalloc_hid_ptr[64];  // device address of g_noalloc_mod_hid per device,
 extern "C" HX_API int hx_modulation_noalloc(const void* modA, const void* modB, const float* emb_dev,
                                             const float* lora_dev, float* mod_dev, int nsite, int D, void* stream) {
   if (!modA || !modB || !emb_dev || !mod_dev || nsite <= 0 || D <= 0 || D % 256) return HX_E_ARG;
+  // the stage kernels read modA / modB rows 16 bytes at a time
+  if ((reinterpret_cast<uintptr_t>(modA) | reinterpret_cast<uintptr_t>(modB)) & 15) return HX_E_ARG;
   if (static_cast<long>(nsite) * 256 > HX_NOALLOC_MOD_HID_FLOATS) return HX_E_SCRATCH;
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HX_E_CUDA;
@@ -286,12 +288,21 @@ extern "C" HX_API int hx_modulation_noalloc(const void* modA, const void* modB, 
     hid = g_noalloc_hid_ptr[dev];
   }
   // Stage 1 writes every hid element stage 2 reads, so nothing needs clearing between calls.
-  const int R = 256, O = 3 * D, t = 256, wpb = t / 32;
+  // cudaLaunchKernel reports the error of its own launch, not one left queued by an earlier call.
+  int R = 256, O = 3 * D;
+  const int t = 256, wpb = t / 32;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  hx::mod_stage1<<<(nsite * R + wpb - 1) / wpb, t, 0, s>>>(static_cast<const __half*>(modA), emb_dev,
-                                                            static_cast<float*>(hid), nsite, D, R);
-  hx::mod_stage2<<<(nsite * O + wpb - 1) / wpb, t, 0, s>>>(static_cast<const __half*>(modB),
-                                                            static_cast<const float*>(hid), lora_dev, mod_dev, nsite,
-                                                            R, O);
-  return cudaGetLastError() == cudaSuccess ? HX_OK : HX_E_CUDA;
+  const __half* A = static_cast<const __half*>(modA);
+  const __half* Bw = static_cast<const __half*>(modB);
+  float* hidf = static_cast<float*>(hid);
+  const float* hidc = hidf;
+  void* a1[] = {&A, &emb_dev, &hidf, &nsite, &D, &R};
+  if (cudaLaunchKernel(reinterpret_cast<const void*>(&hx::mod_stage1), dim3((nsite * R + wpb - 1) / wpb), dim3(t), a1,
+                       0, s) != cudaSuccess)
+    return HX_E_CUDA;
+  void* a2[] = {&Bw, &hidc, &lora_dev, &mod_dev, &nsite, &R, &O};
+  if (cudaLaunchKernel(reinterpret_cast<const void*>(&hx::mod_stage2), dim3((nsite * O + wpb - 1) / wpb), dim3(t), a2,
+                       0, s) != cudaSuccess)
+    return HX_E_CUDA;
+  return HX_OK;
 }

@@ -146,13 +146,16 @@ cudaError_t sp_attention(SpState& sp, const __half* qkv, __half* O, int ldo, int
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
+  // every Send / Recv result is checked; a failed enqueue still closes the group before returning
   if (n.GroupStart() != ncclSuccess) return cudaErrorUnknown;
-  for (int j = 0; j < P; ++j)
-    for (int c = 0; c < 3; ++c) {
-      n.Send(send + (static_cast<size_t>(c) * P + j) * chunk, chunk, ncclHalf, j, comm, s);
-      n.Recv(recv + static_cast<size_t>(c) * P * chunk + static_cast<size_t>(j) * chunk, chunk, ncclHalf, j, comm, s);
+  bool ok = true;
+  for (int j = 0; j < P && ok; ++j)
+    for (int c = 0; c < 3 && ok; ++c) {
+      ok = n.Send(send + (static_cast<size_t>(c) * P + j) * chunk, chunk, ncclHalf, j, comm, s) == ncclSuccess &&
+           n.Recv(recv + static_cast<size_t>(c) * P * chunk + static_cast<size_t>(j) * chunk, chunk, ncclHalf, j,
+                  comm, s) == ncclSuccess;
     }
-  if (n.GroupEnd() != ncclSuccess) return cudaErrorUnknown;
+  if (n.GroupEnd() != ncclSuccess || !ok) return cudaErrorUnknown;
   AttnArgs a;
   a.q = recv;
   a.ldq = Dl;
@@ -171,11 +174,10 @@ cudaError_t sp_attention(SpState& sp, const __half* qkv, __half* O, int ldo, int
   cudaError_t e = attn_launch(a, s);
   if (e != cudaSuccess) return e;
   if (n.GroupStart() != ncclSuccess) return cudaErrorUnknown;
-  for (int j = 0; j < P; ++j) {
-    n.Send(ofull + static_cast<size_t>(j) * chunk, chunk, ncclHalf, j, comm, s);
-    n.Recv(orecv + static_cast<size_t>(j) * chunk, chunk, ncclHalf, j, comm, s);
-  }
-  if (n.GroupEnd() != ncclSuccess) return cudaErrorUnknown;
+  for (int j = 0; j < P && ok; ++j)
+    ok = n.Send(ofull + static_cast<size_t>(j) * chunk, chunk, ncclHalf, j, comm, s) == ncclSuccess &&
+         n.Recv(orecv + static_cast<size_t>(j) * chunk, chunk, ncclHalf, j, comm, s) == ncclSuccess;
+  if (n.GroupEnd() != ncclSuccess || !ok) return cudaErrorUnknown;
   const long total = static_cast<long>(P) * Tl * (Dl / 8);
   sp_unpack_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(orecv, O, Tl, D, P, ldo);
   return cudaGetLastError();

@@ -236,12 +236,15 @@ HX_API int hx_modulation(hx_handle h, int wfd, const float* emb_dev, const float
  * cannot call cudaMalloc: code that runs while another thread captures a CUDA graph in the global
  * capture mode, hosts that run from a fixed, pre-reserved memory pool (as the reference's DSP side runs
  * from a fixed VTCM/rpcmem region), or callers that never open a handle because hx_open allocates.
- * It needs no handle: modA [nsite][256][D] and modB [nsite][3D][256] are fp16 device arrays, emb [D],
- * lora [3D] (may be NULL) and mod [nsite][3D] fp32 device arrays, stream a cudaStream_t (NULL = the
- * legacy default stream) of the current device. The 256-wide hidden vectors live in a static device
+ * It needs no handle: modA [nsite][256][D] and modB [nsite][3D][256] are fp16 device arrays, both
+ * 16-byte aligned (else HX_E_ARG, checked before any launch), emb [D], lora [3D] (may be NULL) and
+ * mod [nsite][3D] fp32 device arrays, stream a cudaStream_t (NULL = the legacy default stream) of the
+ * current device. The 256-wide hidden vectors live in a static device
  * array of 4096 floats (16 KB) that every GPU loading the library holds until the process exits, so
  * nsite * 256 must be <= 4096 (else HX_E_SCRATCH). The first call on a device looks up that array's
- * device address with the device current; make that first call before any stream capture. All calls
+ * device address with the device current; make that first call before any stream capture. That address
+ * is remembered per device index for the life of the process: after cudaDeviceReset on a device, do not
+ * call this function on it again. Returns HX_E_CUDA if either launch is refused. All calls
  * share the array and each call overwrites the part it reads before reading it; calls whose kernels
  * overlap on the GPU (different streams without ordering) race on it. Allocates nothing. */
 HX_API int hx_modulation_noalloc(const void* modA, const void* modB, const float* emb_dev, const float* lora_dev,

@@ -2,8 +2,11 @@
 cudaMalloc (a thread running while another captures a CUDA graph in the global mode, hosts with a fixed
 memory pool, callers without a handle). Its scratch is a static device array shared by every call.
 
-Checked through the C ABI against the handle-based hx_modulation on the same inputs, two calls in a row
-(the second must not see the first one's scratch). This file is collected last on purpose."""
+Checked through the C ABI against the handle-based hx_modulation and against the oracle's modulation
+(megarun.cpp:158-171) on the same inputs, two calls in a row (the second must not see the first one's
+scratch); that free device memory does not move across further calls; and that the host rejects a
+misaligned weight pointer and an oversized request before launching anything. This file is collected
+last on purpose."""
 import pytest
 import torch
 
@@ -24,18 +27,30 @@ def test_modulation_noalloc_matches_handle_version(D):
         stream = h.stream()
         g = torch.Generator().manual_seed(D)
         for call in range(2):
-            emb = torch.randn(D, generator=g).cuda()
-            lora = (0.1 * torch.randn(3 * D, generator=g)).cuda()
+            emb = torch.randn(D, generator=g)
+            lora = 0.1 * torch.randn(3 * D, generator=g)
+            e, l = emb.cuda(), lora.cuda()
             ref = torch.zeros(9 * D + 3 * 256, device="cuda")
-            h.modulation(wfd, emb, lora, ref)
+            h.modulation(wfd, e, l, ref)
             got = torch.full((9 * D,), float("nan"), device="cuda")
-            rt.modulation_noalloc(tA, tB, emb, lora, got, 3, D, stream)
+            rt.modulation_noalloc(tA, tB, e, l, got, 3, D, stream)
             h.sync()
             assert torch.isfinite(got).all(), call
             assert rel(got, ref[:9 * D]) < 1e-5, call
-        with pytest.raises(rt.HxError) as e:  # 17 sites need 17*256 floats, over the 4096 of the static scratch
-            rt.modulation_noalloc(tA, tB, emb, lora, got, 17, D, stream)
-        assert e.value.rc == rt.HX_E_SCRATCH
+            assert rel(got.cpu().view(9, D), oa.modulation(modA, modB, emb, lora)) < 1e-5, call
+        # further calls allocate nothing: free device memory is unchanged (both kernels are loaded by now)
+        h.sync()
+        free0 = torch.cuda.mem_get_info()[0]
+        for _ in range(4):
+            rt.modulation_noalloc(tA, tB, e, l, got, 3, D, stream)
+        h.sync()
+        assert torch.cuda.mem_get_info()[0] == free0
+        with pytest.raises(rt.HxError) as e1:  # 17 sites need 17*256 floats, over the 4096 of the static scratch
+            rt.modulation_noalloc(tA, tB, e, l, got, 17, D, stream)
+        assert e1.value.rc == rt.HX_E_SCRATCH
+        with pytest.raises(rt.HxError) as e2:  # 2 bytes off a 16-byte boundary: refused on the host, no launch
+            rt.modulation_noalloc(tA.data_ptr() + 2, tB, e, l, got, 3, D, stream)
+        assert e2.value.rc == rt.HX_E_ARG
         h.weights_free(wfd)
         assert h.status() == 0
     finally:
