@@ -1056,6 +1056,26 @@ int hx_status(hx_handle hh, int* status) {
   return HX_OK;
 }
 
+int hx_wait_selftest(hx_handle hh, int64_t limit_ns, int arrive, int32_t* rc) {
+  hx_ctx* h = H(hh);
+  // 1 us .. 2 s (the pipelines' own limit)
+  if (!h || !rc || limit_ns < 1000 || limit_ns > 2000000000LL) return HX_E_ARG;
+  std::lock_guard<std::mutex> lk(h->mu);
+  DevGuard g(h->device);
+  *rc = HX_OK;
+  CK(cudaStreamSynchronize(h->stream));
+  CK(cudaMemsetAsync(h->status, 0, sizeof(int), h->stream));
+  CK(hx::wait_selftest_launch(h->status, static_cast<unsigned long long>(limit_ns), arrive ? 1 : 0, h->stream));
+  CK(cudaStreamSynchronize(h->stream));
+  int stv = 0;
+  CK(cudaMemcpy(&stv, h->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (stv) {
+    CK(cudaMemset(h->status, 0, sizeof(int)));
+    *rc = HX_E_TIMEOUT;
+  }
+  return HX_OK;
+}
+
 int hx_status_ptr(hx_handle hh, int** status_dev) {
   if (!hh || !status_dev) return HX_E_ARG;
   *status_dev = H(hh)->status;

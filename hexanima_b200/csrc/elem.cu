@@ -211,7 +211,27 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ s, __half* __restric
   }
 }
 
+// Self-test of the bounded wait (the runtime's analogue of the reference's HMX self-test, which returns
+// rc -77 when its check fails, moss/hexagon/mega/blk.c:112-118,149-155): thread 0 waits on a shared
+// mbarrier of arrival count 1 with a run-time limit; thread 32 arrives on it only when `arrive` is set.
+// Nothing else is in flight, so an expired wait leaves no copy or MMA behind.
+__global__ void wait_selftest_kernel(int* status, unsigned long long limit_ns, int arrive) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (arrive && threadIdx.x == 32) mbar_arrive(&bar);
+  if (threadIdx.x == 0) mbar_wait_limit(&bar, 0, status, 901, limit_ns);
+}
+
 }  // namespace
+
+cudaError_t wait_selftest_launch(int* status, unsigned long long limit_ns, int arrive, cudaStream_t s) {
+  wait_selftest_kernel<<<1, 64, 0, s>>>(status, limit_ns, arrive);
+  return cudaGetLastError();
+}
 
 cudaError_t lnmod_launch(const float* x, __half* h, int rows, int D, const float* shift, const float* scale,
                          long vec_bstride, int rows_per_img, float eps, cudaStream_t s) {

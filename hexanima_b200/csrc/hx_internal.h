@@ -107,6 +107,8 @@ cudaError_t modulation_batch_launch(const __half* const* Atab, const __half* con
 cudaError_t modulation_launch(const __half* Aw, const __half* Bw, const float* emb, const float* lora, float* out,
                               int nsite, int D, int R, int O, cudaStream_t s);
 cudaError_t f32_to_f16_launch(const float* src, __half* dst, size_t n, cudaStream_t s);
+// one CTA whose thread 0 waits with a run-time limit on an mbarrier that is arrived on only if `arrive`
+cudaError_t wait_selftest_launch(int* status, unsigned long long limit_ns, int arrive, cudaStream_t s);
 
 // per-step glue (glue.cu)
 struct Sigmas {

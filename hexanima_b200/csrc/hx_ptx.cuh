@@ -57,16 +57,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete. On timeout it stores `code`
-// into *status (first writer wins) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+// Bounded wait for the phase with the given parity to complete. On timeout (limit_ns of polling)
+// it stores `code` into *status (first writer wins) and returns false.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, int* status, int code,
+                                                uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   uint32_t spins = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 255u) == 0) {
-      if (globaltimer() - t0 > HX_WAIT_LIMIT_NS) {
+      if (globaltimer() - t0 > limit_ns) {
         if (status) atomicCAS(status, 0, code);
         return false;
       }
@@ -74,6 +75,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
       if (status && *reinterpret_cast<volatile int*>(status) != 0) return false;
     }
   }
+}
+// The pipelines' wait: the same, with the fixed limit HX_WAIT_LIMIT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  return mbar_wait_limit(bar, parity, status, code, HX_WAIT_LIMIT_NS);
 }
 
 // ---------------------------------------------------------------- fences

@@ -128,6 +128,7 @@ _SIGS = {
     "hx_sync": [_vp],
     "hx_status": [_vp, ctypes.POINTER(_i)],
     "hx_status_ptr": [_vp, ctypes.POINTER(_vp)],
+    "hx_wait_selftest": [_vp, ctypes.c_int64, _i, _ip],
     "hx_buf_alloc": [_vp, _sz, ctypes.POINTER(_i)],
     "hx_buf_free": [_vp, _i],
     "hx_buf_ptr": [_vp, _i, ctypes.POINTER(_vp)],
@@ -289,6 +290,13 @@ class Handle:
         st = ctypes.c_int()
         _check(lib().hx_status(self.h, ctypes.byref(st)), "hx_status")
         return st.value
+
+    def wait_selftest(self, limit_ns, arrive):
+        """hx_wait_selftest: one bounded device wait with a run-time limit; returns its rc (HX_OK, or
+        HX_E_TIMEOUT when nothing arrived within limit_ns)."""
+        rc = ctypes.c_int32()
+        _check(lib().hx_wait_selftest(self.h, int(limit_ns), 1 if arrive else 0, ctypes.byref(rc)), "hx_wait_selftest")
+        return rc.value
 
     # -------------------------------------------------------------- buffers
     def buf_alloc(self, nbytes):

@@ -69,6 +69,13 @@ HX_API int hx_sync(hx_handle h);
 /* Device status word written by bounded waits (0 = ok, else the code of the wait that expired);
  * reading it synchronises the stream and clears it. */
 HX_API int hx_status(hx_handle h, int* status);
+/* Self-test of the bounded device wait, in the spirit of the reference's HMX self-test that answers
+ * rc -77 when its check fails (moss/hexagon/mega/blk.c:112-118,149-155). One thread waits on a
+ * shared-memory mbarrier with the given limit (1 us .. 2 s); when arrive != 0 another thread arrives on
+ * it and the wait succeeds (*rc = HX_OK), otherwise the wait expires and the kernel returns with the
+ * status word set, which the host reads: *rc = HX_E_TIMEOUT. Nothing else runs in that kernel. The
+ * status word is cleared before and after; the handle stays usable. Synchronises the handle's stream. */
+HX_API int hx_wait_selftest(hx_handle h, int64_t limit_ns, int arrive, int32_t* rc);
 /* Device pointer to the status word, for callers that launch operators on their own streams. */
 HX_API int hx_status_ptr(hx_handle h, int** status_dev);
 
