@@ -208,23 +208,30 @@ def unpatchify(y, H, W, C=16):
     return y.view(B, H // 2, W // 2, 2, 2, C).permute(0, 5, 1, 3, 2, 4).reshape(B, C, H, W)
 
 
-def sample(lat, ctx, cos, sin, blocks, glue, steps=4, sigmas=None):
-    """Full Euler sample of animad.cpp:423-492: blocks = [(W, gain, modA, modB)], glue = glue_init dict.
-    lat [B][16][H][W] fp32 -> denoised latent."""
-    sig = sigmas if sigmas is not None else sigma_schedule(steps)
+def sample_step(lat, sig_i, sig_next, ctx, cos, sin, blocks, glue):
+    """One Euler denoising step of animad.cpp:423-492 at sigma sig_i: timestep embedding, t_embedder,
+    patchify + x_embedder, every block with its modulation, final layer, unpatchify,
+    lat + (sig_next - sig_i) * v. Returns the new latent."""
     B, C, H, Wd = lat.shape
     D = glue["t_lin1"].shape[0]
+    tp, emb = timestep_embedding(sig_i, D, glue["t_norm"])
+    lora = glue["t_lin2"].float() @ torch.nn.functional.silu(glue["t_lin1"].float() @ tp)
+    x = patchify(lat) @ glue["x_emb"].float().T
+    for (W, gain, modA, modB) in blocks:
+        x = block(x, ctx, modulation(modA, modB, emb, lora), cos, sin, W, gain)
+    fm = glue["f_modB"].float() @ (glue["f_modA"].float() @ torch.nn.functional.silu(emb)) + lora[: 2 * D]
+    h = ln_mod(x, fm[:D], fm[D:])
+    v = unpatchify(h @ glue["f_lin"].float().T, H, Wd)
+    return lat + (float(sig_next) - float(sig_i)) * v
+
+
+def sample(lat, ctx, cos, sin, blocks, glue, steps=4, sigmas=None):
+    """Full Euler sample of animad.cpp:423-492: blocks = [(W, gain, modA, modB)] (iterated once per
+    step), glue = glue_init dict. lat [B][16][H][W] fp32 -> denoised latent."""
+    sig = sigmas if sigmas is not None else sigma_schedule(steps)
     lat = lat.clone()
     for i in range(steps):
-        tp, emb = timestep_embedding(sig[i], D, glue["t_norm"])
-        lora = glue["t_lin2"].float() @ torch.nn.functional.silu(glue["t_lin1"].float() @ tp)
-        x = patchify(lat) @ glue["x_emb"].float().T
-        for (W, gain, modA, modB) in blocks:
-            x = block(x, ctx, modulation(modA, modB, emb, lora), cos, sin, W, gain)
-        fm = glue["f_modB"].float() @ (glue["f_modA"].float() @ torch.nn.functional.silu(emb)) + lora[: 2 * D]
-        h = ln_mod(x, fm[:D], fm[D:])
-        v = unpatchify(h @ glue["f_lin"].float().T, H, Wd)
-        lat = lat + (float(sig[i + 1]) - float(sig[i])) * v
+        lat = sample_step(lat, sig[i], sig[i + 1], ctx, cos, sin, blocks, glue)
     return lat
 
 

@@ -76,3 +76,41 @@ def write_f32(h, bfd, off, a):
 
 def read_f32(h, bfd, off, n):
     return np.frombuffer(h.buf_read(bfd, off, n * 4).tobytes(), np.float32).copy()
+
+
+def dequant_q8_torch(u, s, group):
+    """u8 [N][K] offset binary, fp16 scale [K/group][N] (CPU tensors) -> fp32 [N][K] = fp16(q * s): the same
+    values as oracle.packs.dequant_q8 (q * s is exact in fp32, then one round to fp16), multithreaded."""
+    N, K = u.shape
+    q = u.view(N, K // group, group).to(torch.float32) - 128.0
+    return (q * s.float().T.unsqueeze(-1)).half().float().view(N, K)
+
+
+class LazyAnimaBlocks:
+    """The oracle's view of synthetic device weight sets (hexanima_b200.synth): iterating yields
+    (W, gain, modA, modB) per block in oracle naming, each rebuilt on the CPU from the device tensors when
+    it is reached, so host memory holds one block's fp32 weights at a time (oracle.anima.sample iterates
+    the blocks once per denoising step)."""
+
+    def __init__(self, tensors, fmt, D, group=64):
+        self.ts, self.fmt, self.D, self.group = tensors, fmt, D, group
+
+    def __len__(self):
+        return len(self.ts)
+
+    def weights(self, i):
+        t, D = self.ts[i], self.D
+        deq = {}
+        for slot, (w, s) in t["mats"].items():
+            if self.fmt == rt.FMT_Q8:
+                deq[slot] = dequant_q8_torch(w.cpu(), s.cpu(), self.group)
+            else:
+                deq[slot] = w.cpu().float()
+        W = {"sq": deq[rt.W_QKV][:D], "sk": deq[rt.W_QKV][D:2 * D], "sv": deq[rt.W_QKV][2 * D:], "so": deq[rt.W_O],
+             "cq": deq[rt.W_CQ], "ck": deq[rt.W_CKV][:D], "cv": deq[rt.W_CKV][D:], "co": deq[rt.W_CO],
+             "m1": deq[rt.W_M1], "m2": deq[rt.W_M2]}
+        return W, t["gain"].cpu().float(), t["modA"].cpu(), t["modB"].cpu()
+
+    def __iter__(self):
+        for i in range(len(self.ts)):
+            yield self.weights(i)
