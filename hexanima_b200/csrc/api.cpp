@@ -132,6 +132,8 @@ struct hx_ctx {
   cudaStream_t xstream = nullptr;
   cudaEvent_t xev_fork = nullptr, xev_read[2] = {nullptr, nullptr}, xev_ready[2] = {nullptr, nullptr};
   cudaEvent_t ev[34] = {};
+  cudaEvent_t spev[4] = {};  // Ulysses attention parts of the last timed block (times[17..19])
+  bool spev_used = false;
   std::vector<ChainGraph> graphs;
   uint64_t graph_clock = 0;
   std::map<int, std::unique_ptr<Glue>> glues;
@@ -727,7 +729,8 @@ int moss_block(hx_ctx* h, const Weights& W, const int32_t* meta, uint8_t* blob, 
   if (st.tick()) return HX_OK;
   const int sp = meta[HX_S_SP];
   if (sp > 1) {  // Ulysses: token shards -> head shards -> full-sequence attention -> back
-    CKL(hx::sp_attention(h->sp, qkv, obuf, D, T, D, H, nvalid, h->status, s));
+    h->spev_used = st.ntimes > 19;
+    CKL(hx::sp_attention(h->sp, qkv, obuf, D, T, D, H, nvalid, h->status, s, h->spev_used ? h->spev : nullptr));
   } else {
     AttnArgs a;
     a.q = qkv; a.ldq = 3 * D; a.q_col0 = 0;
@@ -968,6 +971,7 @@ int hx_open(int device, hx_handle* out) {
     return HX_E_CUDA;
   }
   for (auto& e : h->ev) cudaEventCreate(&e);
+  for (auto& e : h->spev) cudaEventCreate(&e);
   // side stream and events of the look-ahead weight expansion (without them the chain expands in line)
   if (cudaStreamCreateWithFlags(&h->xstream, cudaStreamNonBlocking) != cudaSuccess) {
     h->xstream = nullptr;
@@ -1013,6 +1017,7 @@ int hx_close(hx_handle hh) {
     h->ms.release();
     cudaFree(h->status);
     for (auto& e : h->ev) cudaEventDestroy(e);
+    for (auto& e : h->spev) cudaEventDestroy(e);
     if (h->own_stream) cudaStreamDestroy(h->stream);
   }
   delete h;
@@ -1420,6 +1425,14 @@ int hx_mega_block(hx_handle hh, const int32_t* meta, int nmeta, int wfd, int bfd
       float ms = 0.f;
       cudaEventElapsedTime(&ms, h->ev[i], h->ev[i + 1]);
       times[i] = static_cast<int32_t>(ms * 1000.f);
+    }
+    if (h->spev_used) {  // Ulysses attention stage: pack + q|k|v exchange, attention, o exchange + unpack
+      for (int i = 0; i < 3; ++i) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, h->spev[i], h->spev[i + 1]);
+        times[17 + i] = static_cast<int32_t>(ms * 1000.f);
+      }
+      h->spev_used = false;
     }
     int stv = 0;
     cudaMemcpy(&stv, h->status, sizeof(int), cudaMemcpyDeviceToHost);

@@ -128,7 +128,7 @@ int sp_reserve(SpState& sp, size_t Tl, size_t D) {
 
 // the Ulysses attention of one block: qkv [Tl][3D] -> O [Tl][D] (row pitch ldo)
 cudaError_t sp_attention(SpState& sp, const __half* qkv, __half* O, int ldo, int Tl, int D, int H, int nvalid,
-                         int* status, cudaStream_t s) {
+                         int* status, cudaStream_t s, cudaEvent_t* ev) {
   NcclApi& n = nccl();
   const int P = sp.nranks;
   if (!n.ok || !sp.comm || P < 2 || H % P || D % (8 * P) || static_cast<size_t>(Tl) * D > sp.cap)
@@ -140,6 +140,7 @@ cudaError_t sp_attention(SpState& sp, const __half* qkv, __half* O, int ldo, int
   __half* ofull = static_cast<__half*>(sp.ofull);
   __half* orecv = static_cast<__half*>(sp.orecv);
   ncclComm_t comm = static_cast<ncclComm_t>(sp.comm);
+  if (ev) cudaEventRecord(ev[0], s);
   {
     const long total = 3L * P * Tl * (Dl / 8);
     sp_pack_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(qkv, send, Tl, D, P);
@@ -156,6 +157,7 @@ cudaError_t sp_attention(SpState& sp, const __half* qkv, __half* O, int ldo, int
                   comm, s) == ncclSuccess;
     }
   if (n.GroupEnd() != ncclSuccess || !ok) return cudaErrorUnknown;
+  if (ev) cudaEventRecord(ev[1], s);
   AttnArgs a;
   a.q = recv;
   a.ldq = Dl;
@@ -173,6 +175,7 @@ cudaError_t sp_attention(SpState& sp, const __half* qkv, __half* O, int ldo, int
   a.status = status;
   cudaError_t e = attn_launch(a, s);
   if (e != cudaSuccess) return e;
+  if (ev) cudaEventRecord(ev[2], s);
   if (n.GroupStart() != ncclSuccess) return cudaErrorUnknown;
   for (int j = 0; j < P && ok; ++j)
     ok = n.Send(ofull + static_cast<size_t>(j) * chunk, chunk, ncclHalf, j, comm, s) == ncclSuccess &&
@@ -180,7 +183,9 @@ cudaError_t sp_attention(SpState& sp, const __half* qkv, __half* O, int ldo, int
   if (n.GroupEnd() != ncclSuccess || !ok) return cudaErrorUnknown;
   const long total = static_cast<long>(P) * Tl * (Dl / 8);
   sp_unpack_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(orecv, O, Tl, D, P, ldo);
-  return cudaGetLastError();
+  e = cudaGetLastError();
+  if (e == cudaSuccess && ev) cudaEventRecord(ev[3], s);
+  return e;
 }
 
 }  // namespace hx

@@ -230,7 +230,9 @@ HX_API int hx_sp_init(hx_handle h, int nranks, int rank, const void* id128);
 /* One DiT block forward: mega_block (hexagon/mega/mega.idl:10). mod: host fp32 modulation
  * (Anima 9*D floats, MOSS 6*D; modlen in bytes) copied per call, or NULL to read it from the blob.
  * times[0..]: per-stage microseconds when ntimes > 0 (synchronises; slot order of the reference's
- * TICKs, times[24] = entry latency). *rc: HX_OK or a negative HX_E* code. */
+ * TICKs, times[24] = entry latency). With meta SP > 1 and ntimes > 19 the attention sub-stage slots
+ * (times[17..22] in the reference, blk.c:178) hold the Ulysses parts: [17] pack + q|k|v all-to-all,
+ * [18] attention on the rank's heads, [19] o all-to-all + unpack. *rc: HX_OK or a negative HX_E* code. */
 HX_API int hx_mega_block(hx_handle h, const int32_t* meta, int nmeta, int wfd, int bfd, const uint8_t* mod, int modlen,
                   int32_t* times, int ntimes, int32_t* rc);
 
