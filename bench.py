@@ -56,7 +56,7 @@ MD, MF, MHEADS, MOSS_H, MOSS_W, MOSS_TXT = 3072, 12288, 24, 64, 64, 512
 # rank, summed over its launches, from `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum` of
 # `python -m hexanima_b200.opbench --ops m1 --batch B` (profiles/gemm_m1_traffic.md). From 3072 rows up a
 # call is the weight expansion plus the fp16 GEMM; below, the q8 GEMM with the dequantisation in its loop.
-TRAFFIC = {}
+TRAFFIC = {1536: 23652352, 3072: 69085696, 6144: 132079360, 12288: 304765440}
 
 
 def _peaks():

@@ -351,6 +351,16 @@ __device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
                : "r"(addr));
   return v;
 }
+// Warpgroup register reallocation (all four warps of a warpgroup execute it): .inc waits until the
+// registers are free, so the sum over warpgroups must fit the block's launch allocation.
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
 __device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
 __device__ __forceinline__ bool elect_one() { return lane_id() == 0; }
 
