@@ -7,16 +7,22 @@
 // The reference folds 1/sqrt(128) into the q RMS gain (export_all.py:31-32), so scale = 1 there.
 //
 // Persistent: one CTA per SM walks items (256 queries = two 128-row Q tiles A and B, head, image), the
-// next item's Q, K and V loads overlapping the current item's softmax. 10 warps:
-//   warps 0-3  softmax of Q tile A, warps 4-7 softmax of Q tile B: thread = one query row (TMEM lane
-//              32(w%4) + lane); the two warps on an SMSP serve different Q tiles, so one's exps
-//              overlap the other's loads and the tensor core's work
-//   warp  8    TMA producer (Q tiles once, then K and V tiles of 128 keys in 2-stage rings)
-//   warp  9    TMEM allocator + tcgen05.mma issuer
+// next item's Q, K and V loads overlapping the current item's softmax. 16 warps in four warpgroups:
+//   warpgroup 0 softmax of Q tile A, warpgroup 1 softmax of Q tile B: thread = one query row (TMEM lane
+//              32(w%4) + lane) with the row's 128 scores of a K tile in registers (one TMEM load wait);
+//              P is published in two parts so the P V MMA starts on keys [0, 96) while the rest is
+//              computed, and the row sum is taken after P is published
+//   warpgroup 2 epilogue: O_X / l of each item to global memory, while the softmax warps go on with the
+//              next item
+//   warpgroup 3 warp 12 TMA producer (Q tiles once, then K and V tiles of 128 keys in 2-stage rings),
+//              warp 13 TMEM allocator + tcgen05.mma issuer, warps 14-15 idle
+// setmaxnreg gives the softmax warpgroups 192 registers, the epilogue 32 and the control warpgroup 96.
 // TMEM columns: S_A [0,128), S_B [128,256) fp32; O_A [256,384), O_B [384,512) fp32 accumulators.
 // P_X (fp16, two per column) is written over columns [0,64) of S_X once they are read, and O_X += P_X V
-// reads it from TMEM. S_X(j+1) overwrites P_X(j), so it is issued only after the commit of
-// O_X += P_X(j) V has arrived (an explicit wait: tcgen05 orders MMAs only on the same accumulator).
+// reads it from TMEM. S_X(j+1) overwrites P_X(j); the MMA thread issues it directly after
+// O_X += P_X(j) V, and the tensor pipe runs the MMAs of one thread in issue order. The commit that
+// signals S_X(j+1) to the softmax warps also covers every earlier MMA, so by then O_X += P_X(j) V is
+// complete and O_X may be rescaled.
 // Online softmax with a lazy reference maximum: P = 2^(s*scale_log2 - m_ref) and the row sum use m_ref,
 // which moves (rescaling the row of O in TMEM and the running sum) only when the tile maximum exceeds
 // it by more than 8, so P <= 256. o = O / l at the end is independent of m_ref.
@@ -36,15 +42,20 @@ namespace {
 
 constexpr int QT = 128, KT = 128, HD = 128;
 constexpr int QPAIR = 2 * QT;  // queries per CTA
-constexpr int SM_WARPS = 8;    // softmax warps
-constexpr int TMA_WARP = SM_WARPS, MMA_WARP = SM_WARPS + 1;
-constexpr int ATT_THREADS = (SM_WARPS + 2) * 32;
+// 16 warps: warpgroups 0 and 1 softmax (Q tiles A and B), 2 epilogue, 3 control (TMA warp, MMA warp, 2 idle)
+constexpr int ATT_WARPS = 16, ATT_THREADS = ATT_WARPS * 32;
+constexpr int EPI_WG = 2;
+constexpr int TMA_WARP = 12, MMA_WARP = 13;
+constexpr int REG_SOFTMAX = 192, REG_EPI = 32, REG_CTRL = 96;  // setmaxnreg split of the 128 a thread starts with
+static_assert(2 * REG_SOFTMAX + REG_EPI + REG_CTRL <= 4 * 128, "register split exceeds the launch allocation");
+constexpr int P_SPLIT = 96;   // keys of P published first (the P V MMA starts on them)
 constexpr int KV_STAGES = 2;
 constexpr int TILE_BYTES = 128 * 128 * 2;  // 32 KB: two 64-column swizzled halves
-// Q_A | Q_B | K0 K1 | V0 V1, then barriers
+// Q_A | Q_B | K0 K1 | V0 V1, then barriers, then the row sums handed to the epilogue
 constexpr int SMEM_Q = 0, SMEM_K = 2 * TILE_BYTES, SMEM_V = SMEM_K + KV_STAGES * TILE_BYTES;
 constexpr int SMEM_BARS = SMEM_V + KV_STAGES * TILE_BYTES;
-constexpr int ATT_SMEM = SMEM_BARS + 256 + 1024;  // + alignment slack
+constexpr int SMEM_L = SMEM_BARS + 256;
+constexpr int ATT_SMEM = SMEM_L + 2 * QT * 4 + 1024;  // + alignment slack
 constexpr uint32_t TM_S = 0, TM_O = 256;
 constexpr float RESCALE_LOG2 = 8.0f;  // move m_ref only when the tile max exceeds it by more than this
 
@@ -166,6 +177,32 @@ __device__ __forceinline__ void exp32(uint32_t (&pk)[16], uint64_t (&sum2)[4], c
   }
 }
 
+// the same exps, kept: r[t] becomes p as fp32 (for the row sum, taken after P is published); no sums here
+template <bool FULL>
+__device__ __forceinline__ void exp32_keep(uint32_t (&pk)[16], uint32_t (&r)[32], uint64_t scale2, uint64_t negm2,
+                                           int kbase, int limit) {
+#pragma unroll
+  for (int t = 0; t < 32; t += 2) {
+    const uint64_t x2 = ffma2(f2pack(__uint_as_float(r[t]), __uint_as_float(r[t + 1])), scale2, negm2);
+    float e0, e1;
+    if (((t >> 1) & kPolyMask) == kPolyMask) {
+      ex2_poly2(x2, e0, e1);
+    } else {
+      float x0, x1;
+      f2unpack(x2, x0, x1);
+      e0 = ex2(x0);
+      e1 = ex2(x1);
+    }
+    if constexpr (!FULL) {
+      if (kbase + t >= limit) e0 = 0.f;
+      if (kbase + t + 1 >= limit) e1 = 0.f;
+    }
+    r[t] = __float_as_uint(e0);
+    r[t + 1] = __float_as_uint(e1);
+    pk[t / 2] = pack_half2(e0, e1);
+  }
+}
+
 // bounded wait whose result is the same in every lane, so the warp-collective tcgen05.ld / st that
 // follow are reached by all lanes or by none
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
@@ -183,15 +220,19 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* k_empty = bars + 3;   // [2]
   uint64_t* v_full = bars + 5;    // [2]
   uint64_t* v_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;    // [Q tile]
-  uint64_t* p_full = bars + 11;   // [Q tile], one arrival per softmax warp of the tile
-  uint64_t* pv_done = bars + 13;  // [Q tile], O_X += P_X V committed
-  uint64_t* drain = bars + 15;
-  uint64_t* q_empty = bars + 16;  // the item's S MMAs have read Q: the next item's Q may load
-  uint64_t* o_free = bars + 17;   // [Q tile], the softmax warps have read O_X: the next item may overwrite it
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 20);
+  uint64_t* s_full = bars + 9;    // [Q tile] S_X(g) committed
+  uint64_t* p_part = bars + 11;   // [Q tile] P_X(g) keys [0, P_SPLIT) stored, one arrival per softmax warp
+  uint64_t* p_full = bars + 13;   // [Q tile] all of P_X(g) stored
+  uint64_t* pv_done = bars + 15;  // [Q tile] O_X += P_X(g) V committed
+  uint64_t* l_full = bars + 17;   // [Q tile] the item's row sums are in sm_l, one arrival per softmax warp
+  uint64_t* l_free = bars + 19;   // [Q tile] the epilogue warps have read them
+  uint64_t* o_free = bars + 21;   // [Q tile] the epilogue warps have read O_X: the next item may overwrite it
+  uint64_t* q_empty = bars + 23;  // the item's S MMAs have read Q: the next item's Q may load
+  uint64_t* drain = bars + 24;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
+  float* sm_l = reinterpret_cast<float*>(smem + SMEM_L);  // [Q tile][128] row sums handed to the epilogue
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wg = warp >> 2;
   const int nkt = p.nkt;
   // persistent: this CTA's items n = 0, 1, ... are blockIdx.x + n * gridDim.x; item -> (Q-tile pair, head,
   // image) with the Q-tile pair fastest so that CTAs running at the same time share K and V in L2
@@ -217,8 +258,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&s_full[x], 1);
+      mbar_init(&p_part[x], 4);
       mbar_init(&p_full[x], 4);
       mbar_init(&pv_done[x], 1);
+      mbar_init(&l_full[x], 4);
+      mbar_init(&l_free[x], 4);
       mbar_init(&o_free[x], 4);
     }
     mbar_init(drain, 1);
@@ -235,6 +279,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   grid_dep_wait();  // the previous kernel's outputs (q, k, v) are complete
   grid_dep_launch();
 
+  // registers: the block starts with 128 per thread (65536); each role branch first sets its warpgroup's
+  // share: softmax 192, epilogue 32, control 96, so 128 threads x (192 + 192 + 32 + 96) = 65536, and per
+  // SMSP (one warp of each warpgroup) 32 x 512 = 16384, its register bank
+  if (wg == 3) {
+    setmaxnreg_dec<REG_CTRL>();
   if (warp == TMA_WARP) {
     if (lane == 0) {
       prefetch_tmap(&tmQ);
@@ -285,10 +334,9 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       constexpr uint32_t id_o = idesc_f16(QT, HD, 0, 1);  // O += P V, P K-major in TMEM, V MN-major
       bool ok = true;
       bool issued = false;
-      // S_x(g): P_x(g-1) (aliasing S_x) must have been read by O_x += P V
-      auto issue_s = [&](int x, int g) -> bool {
-        if (g > 0 && !mbar_wait(&pv_done[x], (g - 1) & 1, p.status, 203)) return false;
-        tc_fence_after();
+      // S_x(g) overwrites P_x(g-1), the A operand of O_x += P_x(g-1) V: it is issued right after that MMA by
+      // this thread, and the tensor pipe runs one thread's MMAs in issue order
+      auto issue_s = [&](int x, int g) {
         const uint32_t q0 = smem_u32(smem + SMEM_Q + x * TILE_BYTES);
         const uint32_t kb = smem_u32(smem + SMEM_K + (g & 1) * TILE_BYTES);
 #pragma unroll
@@ -299,31 +347,41 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         }
         issued = true;
         mma_commit(&s_full[x]);
-        return true;
       };
-      // O_x (+)= P_x(g) V(g); the first tile of an item overwrites O_x once the previous item's O_x was read
+      // O_x (+)= P_x(g) V(g) in two parts: keys [0, P_SPLIT) as soon as the softmax warps have stored them,
+      // the rest when all of P is stored; the first tile of an item overwrites O_x once the previous item's
+      // O_x was read
       auto issue_pv = [&](int x, int g, int n, bool first) -> bool {
-        if (!mbar_wait(&p_full[x], g & 1, p.status, 204)) return false;
         if (first && n > 0 && !mbar_wait(&o_free[x], (n - 1) & 1, p.status, 215)) return false;
-        tc_fence_after();
         const uint32_t vb = smem_u32(smem + SMEM_V + (g & 1) * TILE_BYTES);
+        if (!mbar_wait(&p_part[x], g & 1, p.status, 204)) return false;
+        tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < KT / 16; ++k) {
+        for (int k = 0; k < P_SPLIT / 16; ++k) {
           const uint64_t bd = sdesc_sw128(vb + 2048 * k, TILE_BYTES / 2, 1024);
           mma_f16_ts(tmem + TM_O + x * 128, tmem + TM_S + x * 128 + 8 * k, bd, id_o, (!first || k != 0) ? 1u : 0u);
         }
         issued = true;
+        if (!mbar_wait(&p_full[x], g & 1, p.status, 216)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = P_SPLIT / 16; k < KT / 16; ++k) {
+          const uint64_t bd = sdesc_sw128(vb + 2048 * k, TILE_BYTES / 2, 1024);
+          mma_f16_ts(tmem + TM_O + x * 128, tmem + TM_S + x * 128 + 8 * k, bd, id_o, 1u);
+        }
         mma_commit(&pv_done[x]);
         return true;
       };
       for (int n = 0; n < nmine && ok; ++n) {
         const int g0 = n * nkt;
         // per tile: PV_A(g) S_A(g+1) PV_B(g) S_B(g+1); the item starts with S_A(g0) S_B(g0)
-        if (!(mbar_wait(q_full, n & 1, p.status, 202) && mbar_wait(&k_full[g0 & 1], (g0 >> 1) & 1, p.status, 205) &&
-              issue_s(0, g0) && issue_s(1, g0))) {
+        if (!(mbar_wait(q_full, n & 1, p.status, 202) && mbar_wait(&k_full[g0 & 1], (g0 >> 1) & 1, p.status, 205))) {
           ok = false;
           break;
         }
+        tc_fence_after();
+        issue_s(0, g0);
+        issue_s(1, g0);
         mma_commit(&k_empty[g0 & 1]);
         if (nkt == 1) mma_commit(q_empty);
         for (int j = 0; j < nkt && ok; ++j) {
@@ -331,14 +389,15 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
           const bool more = j + 1 < nkt;
           if (!mbar_wait(&v_full[g & 1], (g >> 1) & 1, p.status, 206)) { ok = false; break; }
           if (!issue_pv(0, g, n, j == 0)) { ok = false; break; }
-          if (more && !(mbar_wait(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, p.status, 207) && issue_s(0, g + 1))) {
-            ok = false;
-            break;
+          if (more) {
+            if (!mbar_wait(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, p.status, 207)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(0, g + 1);
           }
           if (!issue_pv(1, g, n, j == 0)) { ok = false; break; }
           mma_commit(&v_empty[g & 1]);
           if (more) {
-            if (!issue_s(1, g + 1)) { ok = false; break; }
+            issue_s(1, g + 1);
             mma_commit(&k_empty[(g + 1) & 1]);
             if (j + 2 == nkt) mma_commit(q_empty);  // the item's last S is issued: Q may be replaced
           }
@@ -349,19 +408,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         mbar_wait(drain, 0, nullptr, 0);
       }
     }
-  } else {
-    // softmax warps: thread owns query row `row` of Q tile `qx` of each item
-    const int qx = warp >> 2, g4 = warp & 3;
+  }
+  } else if (wg < 2) {
+    setmaxnreg_inc<REG_SOFTMAX>();
+    // softmax warps: thread owns query row `row` of Q tile `qx` of each item, the whole 128-key row of S in
+    // registers
+    const int qx = wg, g4 = warp & 3;
     const int row = g4 * 32 + lane;
     const uint32_t tl = static_cast<uint32_t>(g4 * 32) << 16;
     const uint32_t tS = tmem + tl + TM_S + qx * 128, tO = tmem + tl + TM_O + qx * 128;
     const int limit = p.nvalid;  // keys >= limit are masked
     const uint64_t scale2 = f2pack(p.scale_log2, p.scale_log2);
-    uint32_t sa[32], r[32];
+    uint32_t s[KT];
     bool ok = true;
     for (int n = 0; n < nmine && ok; ++n) {
-      int qp, h, b;
-      item_of(n, qp, h, b);
       float m_ref = 0.f, l_run = 0.f;
       for (int j = 0; j < nkt && ok; ++j) {
         const int g = n * nkt + j;
@@ -369,29 +429,20 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         tc_fence_after();
         const int key0 = j * KT;
         const bool full_tile = key0 + KT <= limit;
-        // row max: keys 64..127 first, then keys 0..63 stay in registers for the exp pass
+        tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(s));
+        tmem_ld32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(s + 32));
+        tmem_ld32(tS + 64, *reinterpret_cast<uint32_t(*)[32]>(s + 64));
+        tmem_ld32(tS + 96, *reinterpret_cast<uint32_t(*)[32]>(s + 96));
+        tmem_ld_wait();
         float mxp[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) mxp[t] = -INFINITY;
-        tmem_ld32(tS + 64, sa);
-        tmem_ld32(tS + 96, r);
-        tmem_ld_wait();
-        if (full_tile) {
-          max32<true>(mxp, sa, key0 + 64, limit);
-          max32<true>(mxp, r, key0 + 96, limit);
-        } else {
-          max32<false>(mxp, sa, key0 + 64, limit);
-          max32<false>(mxp, r, key0 + 96, limit);
-        }
-        tmem_ld32(tS, sa);
-        tmem_ld32(tS + 32, r);
-        tmem_ld_wait();
-        if (full_tile) {
-          max32<true>(mxp, sa, key0, limit);
-          max32<true>(mxp, r, key0 + 32, limit);
-        } else {
-          max32<false>(mxp, sa, key0, limit);
-          max32<false>(mxp, r, key0 + 32, limit);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          if (full_tile)
+            max32<true>(mxp, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c), key0 + 32 * c, limit);
+          else
+            max32<false>(mxp, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c), key0 + 32 * c, limit);
         }
         const float mt =
             fmax3(fmax3(mxp[0], mxp[1], mxp[2]), fmax3(mxp[3], mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])) * p.scale_log2;
@@ -400,100 +451,107 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         } else {
           const bool need = mt > m_ref + RESCALE_LOG2;
           if (__any_sync(0xffffffffu, need)) {
-            // O_X += P_X(g-1) V has completed (S_X(g) was issued after it); P_X(g) is not published yet
+            // O_X += P_X(g-1) V has completed (the s_full commit of S_X(g), issued after it, covers it);
+            // P_X(g) is not published yet
             const float alpha = need ? ex2(m_ref - mt) : 1.f;
             if (need) m_ref = mt;
             l_run *= alpha;
             const uint64_t a2 = f2pack(alpha, alpha);
-            uint32_t ob[32];
+            uint32_t ob[16];  // 16 columns at a time: the row of S stays live in registers meanwhile
 #pragma unroll
-            for (int c = 0; c < HD / 32; ++c) {
-              tmem_ld32(tO + 32 * c, ob);
+            for (int c = 0; c < HD / 16; ++c) {
+              tmem_ld16(tO + 16 * c, ob);
               tmem_ld_wait();
-              uint32_t w0[16], w1[16];
 #pragma unroll
-              for (int t = 0; t < 8; ++t) {
+              for (int t = 0; t < 16; t += 2) {
                 float x0, x1;
-                f2unpack(ffma2(f2pack(__uint_as_float(ob[2 * t]), __uint_as_float(ob[2 * t + 1])), a2, 0ull), x0, x1);
-                w0[2 * t] = __float_as_uint(x0);
-                w0[2 * t + 1] = __float_as_uint(x1);
-                f2unpack(ffma2(f2pack(__uint_as_float(ob[16 + 2 * t]), __uint_as_float(ob[17 + 2 * t])), a2, 0ull),
-                         x0, x1);
-                w1[2 * t] = __float_as_uint(x0);
-                w1[2 * t + 1] = __float_as_uint(x1);
+                f2unpack(ffma2(f2pack(__uint_as_float(ob[t]), __uint_as_float(ob[t + 1])), a2, 0ull), x0, x1);
+                ob[t] = __float_as_uint(x0);
+                ob[t + 1] = __float_as_uint(x1);
               }
-              tmem_st16(tO + 32 * c, w0);
-              tmem_st16(tO + 32 * c + 16, w1);
+              tmem_st16(tO + 16 * c, ob);
             }
           }
         }
         const uint64_t negm2 = f2pack(-m_ref, -m_ref);
-        uint64_t sum2[4] = {0, 0, 0, 0};
-        {
-          // keys 0..63 (registers) -> P columns 0..31, then keys 64..127 -> P columns 32..63; each P column
-          // overwrites S columns this thread has already read
+        // 32 keys at a time: the probabilities go back into s (fp32, for the row sum) and, fp16-packed, into
+        // P columns 16c .. 16c+15 over S columns already read; keys [0, P_SPLIT) are published first
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
           uint32_t pk[16];
-          if (full_tile) {
-            exp32<true>(pk, sum2, sa, scale2, negm2, key0, limit);
-            tmem_st16(tS, pk);
-            exp32<true>(pk, sum2, r, scale2, negm2, key0 + 32, limit);
-            tmem_st16(tS + 16, pk);
-          } else {
-            exp32<false>(pk, sum2, sa, scale2, negm2, key0, limit);
-            tmem_st16(tS, pk);
-            exp32<false>(pk, sum2, r, scale2, negm2, key0 + 32, limit);
-            tmem_st16(tS + 16, pk);
-          }
-          tmem_ld32(tS + 64, sa);
-          tmem_ld32(tS + 96, r);
-          tmem_ld_wait();
-          if (full_tile) {
-            exp32<true>(pk, sum2, sa, scale2, negm2, key0 + 64, limit);
-            tmem_st16(tS + 32, pk);
-            exp32<true>(pk, sum2, r, scale2, negm2, key0 + 96, limit);
-            tmem_st16(tS + 48, pk);
-          } else {
-            exp32<false>(pk, sum2, sa, scale2, negm2, key0 + 64, limit);
-            tmem_st16(tS + 32, pk);
-            exp32<false>(pk, sum2, r, scale2, negm2, key0 + 96, limit);
-            tmem_st16(tS + 48, pk);
+          if (full_tile)
+            exp32_keep<true>(pk, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c), scale2, negm2, key0 + 32 * c, limit);
+          else
+            exp32_keep<false>(pk, *reinterpret_cast<uint32_t(*)[32]>(s + 32 * c), scale2, negm2, key0 + 32 * c, limit);
+          tmem_st16(tS + 16 * c, pk);
+          if (32 * (c + 1) == P_SPLIT || c == 3) {
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(c == 3 ? &p_full[qx] : &p_part[qx]);
           }
         }
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[qx]);
+        // row sum of this tile's probabilities, off the path to the P V MMA
+        uint64_t sum2[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int t = 0; t < KT; t += 2)
+          sum2[(t >> 1) & 3] = fadd2(sum2[(t >> 1) & 3], f2pack(__uint_as_float(s[t]), __uint_as_float(s[t + 1])));
         const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
         float slo, shi;
         f2unpack(s01, slo, shi);
         l_run += slo + shi;
       }
       if (!ok) break;
-      // the item's last O_X += P_X V: earlier ones completed before its last S_X was issued
-      if (!warp_wait(&pv_done[qx], (n * nkt + nkt - 1) & 1, p.status, 209)) { ok = false; break; }
-      tc_fence_after();
-      const int q = qp * QPAIR + qx * QT + row;
-      const bool live = q < p.Tq;
-      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-      uint4* d4 = reinterpret_cast<uint4*>(p.o + (static_cast<size_t>(b) * p.Tq + (live ? q : 0)) * p.ldo + h * HD);
+      // hand the item's row sums to the epilogue warps once they have read the previous item's
+      if (n > 0 && !warp_wait(&l_free[qx], (n - 1) & 1, p.status, 210)) { ok = false; break; }
+      sm_l[qx * QT + row] = l_run;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&l_full[qx]);
+    }
+  } else {
+    setmaxnreg_dec<REG_EPI>();
+    // epilogue warps: O_X / l of each item to global memory; warp 8 + g4 reads TMEM lanes 32 g4 .. +31
+    const int g4 = warp & 3;
+    const int row = g4 * 32 + lane;
+    const uint32_t tl = static_cast<uint32_t>(g4 * 32) << 16;
+    uint32_t ob[16];
+    bool ok = true;
+    for (int n = 0; n < nmine && ok; ++n) {
+      int qp, h, b;
+      item_of(n, qp, h, b);
+      for (int x = 0; x < 2; ++x) {
+        // the row sums first: the softmax warps publish them after the item's last S_X, so the item's P V
+        // commits before the last have all arrived and the pv_done wait below is for the last one
+        if (!warp_wait(&l_full[x], n & 1, p.status, 217)) { ok = false; break; }
+        const float l = sm_l[x * QT + row];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&l_free[x]);
+        if (!warp_wait(&pv_done[x], (n * nkt + nkt - 1) & 1, p.status, 209)) { ok = false; break; }
+        tc_fence_after();
+        const int q = qp * QPAIR + x * QT + row;
+        const bool live = q < p.Tq;
+        const float inv = l > 0.f ? 1.0f / l : 0.f;
+        uint4* d4 = reinterpret_cast<uint4*>(p.o + (static_cast<size_t>(b) * p.Tq + (live ? q : 0)) * p.ldo + h * HD);
+        const uint32_t tO = tmem + tl + TM_O + x * 128;
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        tmem_ld32(tO + 32 * c, sa);
-        tmem_ld_wait();
-        if (c == HD / 32 - 1) {  // all of O_X read: the next item's first P V may overwrite it
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&o_free[qx]);
-        }
-        if (live) {
+        for (int c = 0; c < HD / 16; ++c) {  // 16 columns at a time (56 registers)
+          tmem_ld16(tO + 16 * c, ob);
+          tmem_ld_wait();
+          if (c == HD / 16 - 1) {  // all of O_X read: the next item's first P V may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&o_free[x]);
+          }
+          if (live) {
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const uint32_t* v = sa + 8 * u;
-            d4[4 * c + u] = make_uint4(
-                pack_half2(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv),
-                pack_half2(__uint_as_float(v[2]) * inv, __uint_as_float(v[3]) * inv),
-                pack_half2(__uint_as_float(v[4]) * inv, __uint_as_float(v[5]) * inv),
-                pack_half2(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv));
+            for (int u = 0; u < 2; ++u) {
+              const uint32_t* v = ob + 8 * u;
+              d4[2 * c + u] = make_uint4(
+                  pack_half2(__uint_as_float(v[0]) * inv, __uint_as_float(v[1]) * inv),
+                  pack_half2(__uint_as_float(v[2]) * inv, __uint_as_float(v[3]) * inv),
+                  pack_half2(__uint_as_float(v[4]) * inv, __uint_as_float(v[5]) * inv),
+                  pack_half2(__uint_as_float(v[6]) * inv, __uint_as_float(v[7]) * inv));
+            }
           }
         }
       }
