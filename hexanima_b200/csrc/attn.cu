@@ -14,7 +14,7 @@
 //              computed, and the row sum is taken after P is published
 //   warpgroup 2 epilogue: O_X / l of each item to global memory, while the softmax warps go on with the
 //              next item
-//   warpgroup 3 warp 12 TMA producer (Q tiles once, then K and V tiles of 128 keys in 2-stage rings),
+//   warpgroup 3 warp 12 TMA producer (Q tiles once, then K and V tiles of 128 keys in 2- and 3-stage rings),
 //              warp 13 TMEM allocator + tcgen05.mma issuer, warps 14-15 idle
 // setmaxnreg gives the softmax warpgroups 192 registers, the epilogue 32 and the control warpgroup 96.
 // TMEM columns: S_A [0,128), S_B [128,256) fp32; O_A [256,384), O_B [384,512) fp32 accumulators.
@@ -49,11 +49,11 @@ constexpr int TMA_WARP = 12, MMA_WARP = 13;
 constexpr int REG_SOFTMAX = 192, REG_EPI = 32, REG_CTRL = 96;  // setmaxnreg split of the 128 a thread starts with
 static_assert(2 * REG_SOFTMAX + REG_EPI + REG_CTRL <= 4 * 128, "register split exceeds the launch allocation");
 constexpr int P_SPLIT = 96;   // keys of P published first (the P V MMA starts on them)
-constexpr int KV_STAGES = 2;
+constexpr int K_STAGES = 2, V_STAGES = 3;  // V waits longer for its ring slot (freed by P V, not by S)
 constexpr int TILE_BYTES = 128 * 128 * 2;  // 32 KB: two 64-column swizzled halves
-// Q_A | Q_B | K0 K1 | V0 V1, then barriers, then the row sums handed to the epilogue
-constexpr int SMEM_Q = 0, SMEM_K = 2 * TILE_BYTES, SMEM_V = SMEM_K + KV_STAGES * TILE_BYTES;
-constexpr int SMEM_BARS = SMEM_V + KV_STAGES * TILE_BYTES;
+// Q_A | Q_B | K0 K1 | V0 V1 V2, then barriers, then the row sums handed to the epilogue
+constexpr int SMEM_Q = 0, SMEM_K = 2 * TILE_BYTES, SMEM_V = SMEM_K + K_STAGES * TILE_BYTES;
+constexpr int SMEM_BARS = SMEM_V + V_STAGES * TILE_BYTES;
 constexpr int SMEM_L = SMEM_BARS + 256;
 constexpr int ATT_SMEM = SMEM_L + 2 * QT * 4 + 1024;  // + alignment slack
 constexpr uint32_t TM_S = 0, TM_O = 256;
@@ -218,18 +218,18 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;    // [2]
   uint64_t* k_empty = bars + 3;   // [2]
-  uint64_t* v_full = bars + 5;    // [2]
-  uint64_t* v_empty = bars + 7;   // [2]
-  uint64_t* s_full = bars + 9;    // [Q tile] S_X(g) committed
-  uint64_t* p_part = bars + 11;   // [Q tile] P_X(g) keys [0, P_SPLIT) stored, one arrival per softmax warp
-  uint64_t* p_full = bars + 13;   // [Q tile] all of P_X(g) stored
-  uint64_t* pv_done = bars + 15;  // [Q tile] O_X += P_X(g) V committed
-  uint64_t* l_full = bars + 17;   // [Q tile] the item's row sums are in sm_l, one arrival per softmax warp
-  uint64_t* l_free = bars + 19;   // [Q tile] the epilogue warps have read them
-  uint64_t* o_free = bars + 21;   // [Q tile] the epilogue warps have read O_X: the next item may overwrite it
-  uint64_t* q_empty = bars + 23;  // the item's S MMAs have read Q: the next item's Q may load
-  uint64_t* drain = bars + 24;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 26);
+  uint64_t* v_full = bars + 5;    // [3]
+  uint64_t* v_empty = bars + 8;   // [3]
+  uint64_t* s_full = bars + 11;   // [Q tile] S_X(g) committed
+  uint64_t* p_part = bars + 13;   // [Q tile] P_X(g) keys [0, P_SPLIT) stored, one arrival per softmax warp
+  uint64_t* p_full = bars + 15;   // [Q tile] all of P_X(g) stored
+  uint64_t* pv_done = bars + 17;  // [Q tile] O_X += P_X(g) V committed
+  uint64_t* l_full = bars + 19;   // [Q tile] the item's row sums are in sm_l, one arrival per softmax warp
+  uint64_t* l_free = bars + 21;   // [Q tile] the epilogue warps have read them
+  uint64_t* o_free = bars + 23;   // [Q tile] the epilogue warps have read O_X: the next item may overwrite it
+  uint64_t* q_empty = bars + 25;  // the item's S MMAs have read Q: the next item's Q may load
+  uint64_t* drain = bars + 26;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 28);
   float* sm_l = reinterpret_cast<float*>(smem + SMEM_L);  // [Q tile][128] row sums handed to the epilogue
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, wg = warp >> 2;
@@ -250,9 +250,11 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int i = 0; i < KV_STAGES; ++i) {
+    for (int i = 0; i < K_STAGES; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < V_STAGES; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
@@ -305,27 +307,28 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         ++nq;
         for (int j = 0; j < nkt; ++j) {
           const int g = n * nkt + j;
-          const int st = g & 1, ph = (g >> 1) & 1;
+          const int st = g & 1, ph = (g >> 1) & 1;          // K ring
+          const int vs = g % V_STAGES, vph = (g / V_STAGES) & 1;  // V ring
           uint8_t* kb = smem + SMEM_K + st * TILE_BYTES;
-          uint8_t* vb = smem + SMEM_V + st * TILE_BYTES;
+          uint8_t* vb = smem + SMEM_V + vs * TILE_BYTES;
           if (!mbar_wait(&k_empty[st], ph ^ 1, p.status, 201)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
           tma_load_3d(kb, &tmK, &k_full[st], kc, j * KT, b);
           tma_load_3d(kb + TILE_BYTES / 2, &tmK, &k_full[st], kc + 64, j * KT, b);
           ++nk;
-          if (!mbar_wait(&v_empty[st], ph ^ 1, p.status, 211)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-          tma_load_3d(vb, &tmV, &v_full[st], vc, j * KT, b);
-          tma_load_3d(vb + TILE_BYTES / 2, &tmV, &v_full[st], vc + 64, j * KT, b);
+          if (!mbar_wait(&v_empty[vs], vph ^ 1, p.status, 211)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[vs], TILE_BYTES);
+          tma_load_3d(vb, &tmV, &v_full[vs], vc, j * KT, b);
+          tma_load_3d(vb + TILE_BYTES / 2, &tmV, &v_full[vs], vc + 64, j * KT, b);
           ++nv;
         }
       }
       if (!ok) {  // aborted: let the copies in flight land before the CTA exits
         if (nq > 0) mbar_wait(q_full, (nq - 1) & 1, nullptr, 0);
-        for (int i = (nk > KV_STAGES ? nk - KV_STAGES : 0); i < nk; ++i)
+        for (int i = (nk > K_STAGES ? nk - K_STAGES : 0); i < nk; ++i)
           mbar_wait(&k_full[i & 1], (i >> 1) & 1, nullptr, 0);
-        for (int i = (nv > KV_STAGES ? nv - KV_STAGES : 0); i < nv; ++i)
-          mbar_wait(&v_full[i & 1], (i >> 1) & 1, nullptr, 0);
+        for (int i = (nv > V_STAGES ? nv - V_STAGES : 0); i < nv; ++i)
+          mbar_wait(&v_full[i % V_STAGES], (i / V_STAGES) & 1, nullptr, 0);
       }
     }
   } else if (warp == MMA_WARP) {
@@ -353,7 +356,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
       // O_x was read
       auto issue_pv = [&](int x, int g, int n, bool first) -> bool {
         if (first && n > 0 && !mbar_wait(&o_free[x], (n - 1) & 1, p.status, 215)) return false;
-        const uint32_t vb = smem_u32(smem + SMEM_V + (g & 1) * TILE_BYTES);
+        const uint32_t vb = smem_u32(smem + SMEM_V + (g % V_STAGES) * TILE_BYTES);
         if (!mbar_wait(&p_part[x], g & 1, p.status, 204)) return false;
         tc_fence_after();
 #pragma unroll
@@ -387,7 +390,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
         for (int j = 0; j < nkt && ok; ++j) {
           const int g = g0 + j;
           const bool more = j + 1 < nkt;
-          if (!mbar_wait(&v_full[g & 1], (g >> 1) & 1, p.status, 206)) { ok = false; break; }
+          if (!mbar_wait(&v_full[g % V_STAGES], (g / V_STAGES) & 1, p.status, 206)) { ok = false; break; }
           if (!issue_pv(0, g, n, j == 0)) { ok = false; break; }
           if (more) {
             if (!mbar_wait(&k_full[(g + 1) & 1], ((g + 1) >> 1) & 1, p.status, 207)) { ok = false; break; }
@@ -395,7 +398,7 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
             issue_s(0, g + 1);
           }
           if (!issue_pv(1, g, n, j == 0)) { ok = false; break; }
-          mma_commit(&v_empty[g & 1]);
+          mma_commit(&v_empty[g % V_STAGES]);
           if (more) {
             issue_s(1, g + 1);
             mma_commit(&k_empty[(g + 1) & 1]);
