@@ -764,11 +764,34 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM of the pair allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_base_slot;
-  grid_dep_wait();  // the previous kernel's outputs (A, x) are complete
-  grid_dep_launch();
-
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int row0 = static_cast<int>(rank) * HALF;
+  // Quantised weight tiles and scales are constant during inference (no kernel that can precede this one
+  // with programmatic dependent launch writes them; fp16 weights can be an expansion just before, so they
+  // wait), so the producer loads the first ring of them before waiting for the previous kernel.
+  int npre = 0;
+  if constexpr (FMT != WF_F16) {
+    if (warp == TMA_WARP && lane == 0) {
+      Sched sched(p, pair, npairs);
+      int t, kb0, kb1;
+      if (sched.next(p, t, kb0, kb1)) {
+        const uint32_t sc_rows = BK / p.group;
+        const uint32_t raw_tx = C::RAW_B + sc_rows * HALF * 2 * (FMT == WF_Q4A ? 2 : 1);
+        const int n0 = tile_n(p, t) * BN + row0;
+        npre = kb1 - kb0 < S ? kb1 - kb0 : S;
+        for (int i = 0; i < npre; ++i) {  // stages i are empty on the first pass
+          const int kb = kb0 + i;
+          mbar_arrive_expect_tx(&raw_full[i], raw_tx);
+          tma_load_2d(st_raw(i), &tmW, &raw_full[i], FMT == WF_Q8 ? kb * BK : kb * (BK / 2), n0);
+          tma_load_2d(st_sc(i), &tmS, &raw_full[i], n0, kb * static_cast<int>(sc_rows));
+          if constexpr (FMT == WF_Q4A)
+            tma_load_2d(st_sc(i) + 2 * HALF * 2, &tmMin, &raw_full[i], n0, kb * static_cast<int>(sc_rows));
+        }
+      }
+    }
+  }
+  grid_dep_wait();  // the previous kernel's outputs (A, x) are complete
+  grid_dep_launch();
 
   if (warp == TMA_WARP) {
     if (lane == 0) {
@@ -790,7 +813,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           else tma_load_2d_pair(st_a(s), &tmA2, &full_a[s], (kb - p.nkb1) * BK, m0);
           if constexpr (FMT == WF_F16) {
             tma_load_2d_pair(st_w(s), &tmW, &full_a[s], kb * BK, n0);
-          } else {
+          } else if (it >= npre) {  // the first npre were loaded before the dependency wait
             mbar_arrive_expect_tx(&raw_full[s], raw_tx);
             tma_load_2d(st_raw(s), &tmW, &raw_full[s], FMT == WF_Q8 ? kb * BK : kb * (BK / 2), n0);
             tma_load_2d(st_sc(s), &tmS, &raw_full[s], n0, kb * static_cast<int>(sc_rows));

@@ -291,11 +291,25 @@ __global__ void __launch_bounds__(WT_THREADS, 1)
   cluster_sync();  // barriers of both CTAs initialised, TMEM of the pair allocated
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  grid_dep_wait();  // the previous kernel's outputs (the token rows) are complete
-  grid_dep_launch();
-
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   const int ntiles_mine = p.num_tiles > pair ? (p.num_tiles - 1 - pair) / npairs + 1 : 0;
+  // The raw weight tiles and scales are constant during inference (no kernel that can precede this one
+  // with programmatic dependent launch writes them), so the producer loads the first ring of them before
+  // waiting for the previous kernel; everything else waits first.
+  const bool early_weights = warp == TMA_WARP && lane == 0;
+  const int npre = ntiles_mine > 0 ? (p.nkb < S ? p.nkb : S) : 0;
+  if (early_weights && npre > 0) {
+    const uint32_t sc_rows = WT_BK / p.group;
+    const uint32_t raw_tx = RAW_B + sc_rows * WT_ROWS * 2;
+    const int w0 = wt_tile_n(p, pair) * 2 * WT_ROWS + static_cast<int>(rank) * WT_ROWS;
+    for (int kb = 0; kb < npre; ++kb) {  // stages kb are empty on the first pass
+      mbar_arrive_expect_tx(&raw_full[kb], raw_tx);
+      tma_load_2d(st_raw(kb), &tmW, &raw_full[kb], kb * WT_BK, w0);
+      tma_load_2d(st_sc(kb), &tmS, &raw_full[kb], w0, kb * static_cast<int>(sc_rows));
+    }
+  }
+  grid_dep_wait();  // the previous kernel's outputs (the token rows) are complete
+  grid_dep_launch();
 
   if (warp == TMA_WARP) {
     if (lane == 0) {
@@ -314,6 +328,7 @@ __global__ void __launch_bounds__(WT_THREADS, 1)
           if (leader) mbar_arrive_expect_tx(&full_x[s], 2u * X_B);
           if (kb < p.nkb1) tma_load_2d_pair(st_x(s), &tmA, &full_x[s], kb * WT_BK, tok0);
           else tma_load_2d_pair(st_x(s), &tmA2, &full_x[s], (kb - p.nkb1) * WT_BK, tok0);
+          if (it < npre) continue;  // loaded before the dependency wait
           mbar_arrive_expect_tx(&raw_full[s], raw_tx);
           tma_load_2d(st_raw(s), &tmW, &raw_full[s], kb * WT_BK, w0);
           tma_load_2d(st_sc(s), &tmS, &raw_full[s], w0, kb * static_cast<int>(sc_rows));
