@@ -16,7 +16,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "libhxdit.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
-SOURCES = ["gemm.cu", "gemm_wt.cu", "attn.cu", "elem.cu", "repack.cu", "glue.cu", "sp.cu", "lora.cu", "lorasvd.cu", "adapter.cu", "expand.cu", "api.cpp"]
+SOURCES = ["gemm.cu", "gemm_wt.cu", "attn.cu", "attn_short.cu", "elem.cu", "repack.cu", "glue.cu", "sp.cu", "lora.cu", "lorasvd.cu", "adapter.cu", "expand.cu", "api.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "-I" + os.path.join(ROOT, "include")]
 

@@ -2124,6 +2124,7 @@ int hx_attention(hx_handle hh, const hx_attn_desc* d) {
   a.Tk = d->tk;
   a.nvalid = d->nvalid;
   a.scale = d->scale;
+  a.kernel = d->kernel;
   a.status = h->status;
   cudaError_t e = attn_launch(a, h->stream);
   return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);

@@ -27,10 +27,12 @@
 // which moves (rescaling the row of O in TMEM and the running sum) only when the tile maximum exceeds
 // it by more than 8, so P <= 256. o = O / l at the end is independent of m_ref.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "hx_internal.h"
 #include "hx_ptx.cuh"
+#include "hx_softmax.cuh"
 
 namespace hx {
 
@@ -39,6 +41,8 @@ bool make_tmap_3d(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void*
                   CUtensorMapSwizzle sw);
 
 namespace {
+
+using namespace smx;
 
 constexpr int QT = 128, KT = 128, HD = 128;
 constexpr int QPAIR = 2 * QT;  // queries per CTA
@@ -59,13 +63,6 @@ constexpr int ATT_SMEM = SMEM_L + 2 * QT * 4 + 1024;  // + alignment slack
 constexpr uint32_t TM_S = 0, TM_O = 256;
 constexpr float RESCALE_LOG2 = 8.0f;  // move m_ref only when the tile max exceeds it by more than this
 
-// one MUFU op: 2^x (flush-to-zero; the inputs here are <= 0 and the results feed fp16 probabilities)
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
 struct AParams {
   int Tq, Tk, nvalid, H, nkt;
   int B, nqp;  // images, 256-query blocks per image
@@ -74,140 +71,6 @@ struct AParams {
   int ldo;
   int* status;
 };
-
-// packed fp32 pairs (sm_100 f32x2 arithmetic: two lanes per instruction, each rounded like the scalar op)
-__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-// three-input maximum (sm_100); like fmaxf, a NaN operand is ignored
-__device__ __forceinline__ float fmax3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-__device__ __forceinline__ uint64_t fadd2_rm(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-
-// 2^x for a pair, on the FMA and integer pipes instead of MUFU (relieves the MUFU pipe, which two
-// softmax warps share per SMSP). x = n + f with n = floor(x): adding 1.5*2^23 rounded toward -inf
-// leaves n in the low mantissa bits of the sum, subtracting it back gives n exactly and f = x - n is
-// exact. 2^f on [0, 1) is the cubic 1 + c1 f + c2 f^2 + c3 f^3 fitted for this kernel by linear-
-// programming minimax of the relative error (8.6e-5 in fp32 Horner evaluation; an fp16 half-ulp is
-// 4.9e-4). 2^n is added into the exponent field: the sum's bit pattern is 0x4B400000 + n, and shifted
-// left by 23 it is n << 23 (mod 2^32). Inputs are clamped at -127; results below 2^-126 are far
-// under the fp16 range of P anyway.
-constexpr float kRoundFloor = 12582912.0f;  // 1.5 * 2^23
-constexpr float kExp2C1 = 0.695116639f, kExp2C2 = 0.22764498f, kExp2C3 = 0.0770672411f;
-__device__ __forceinline__ void ex2_poly2(uint64_t x2, float& e0, float& e1) {
-  float x0, x1;
-  f2unpack(x2, x0, x1);
-  const uint64_t xc = f2pack(fmaxf(x0, -127.f), fmaxf(x1, -127.f));
-  const uint64_t t = fadd2_rm(xc, f2pack(kRoundFloor, kRoundFloor));
-  const uint64_t n = fadd2(t, f2pack(-kRoundFloor, -kRoundFloor));
-  const uint64_t fr = ffma2(n, f2pack(-1.f, -1.f), xc);
-  uint64_t q = ffma2(fr, f2pack(kExp2C3, kExp2C3), f2pack(kExp2C2, kExp2C2));
-  q = ffma2(q, fr, f2pack(kExp2C1, kExp2C1));
-  q = ffma2(q, fr, f2pack(1.f, 1.f));
-  float q0, q1, t0, t1;
-  f2unpack(q, q0, q1);
-  f2unpack(t, t0, t1);
-  e0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
-  e1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
-}
-
-// which fp16 pairs of a 32-key chunk take ex2_poly2 instead of MUFU: pair index pi with
-// (pi & kPolyMask) == kPolyMask (kPolyMask 3: one pair in four)
-constexpr int kPolyMask = 3;
-
-// max over 32 raw scores at keys kbase..kbase+31 into 8 partial maxima (keys >= limit skipped)
-template <bool FULL>
-__device__ __forceinline__ void max32(float (&mxp)[8], const uint32_t (&r)[32], int kbase, int limit) {
-  if constexpr (FULL) {
-#pragma unroll
-    for (int t = 0; t < 32; t += 2)
-      mxp[(t >> 1) & 7] = fmax3(mxp[(t >> 1) & 7], __uint_as_float(r[t]), __uint_as_float(r[t + 1]));
-  } else {
-#pragma unroll
-    for (int t = 0; t < 32; ++t)
-      if (kbase + t < limit) mxp[t & 7] = fmaxf(mxp[t & 7], __uint_as_float(r[t]));
-  }
-}
-
-// p = 2^(s*scale_log2 - m) for 32 scores, fp16-packed into pk, pairwise partial sums into sum2
-template <bool FULL>
-__device__ __forceinline__ void exp32(uint32_t (&pk)[16], uint64_t (&sum2)[4], const uint32_t (&r)[32],
-                                      uint64_t scale2, uint64_t negm2, int kbase, int limit) {
-#pragma unroll
-  for (int t = 0; t < 32; t += 2) {
-    const uint64_t x2 = ffma2(f2pack(__uint_as_float(r[t]), __uint_as_float(r[t + 1])), scale2, negm2);
-    float e0, e1;
-    if (((t >> 1) & kPolyMask) == kPolyMask) {
-      ex2_poly2(x2, e0, e1);
-    } else {
-      float x0, x1;
-      f2unpack(x2, x0, x1);
-      e0 = ex2(x0);
-      e1 = ex2(x1);
-    }
-    if constexpr (!FULL) {
-      if (kbase + t >= limit) e0 = 0.f;
-      if (kbase + t + 1 >= limit) e1 = 0.f;
-    }
-    sum2[(t >> 1) & 3] = fadd2(sum2[(t >> 1) & 3], f2pack(e0, e1));
-    pk[t / 2] = pack_half2(e0, e1);
-  }
-}
-
-// the same exps, kept: r[t] becomes p as fp32 (for the row sum, taken after P is published); no sums here
-template <bool FULL>
-__device__ __forceinline__ void exp32_keep(uint32_t (&pk)[16], uint32_t (&r)[32], uint64_t scale2, uint64_t negm2,
-                                           int kbase, int limit) {
-#pragma unroll
-  for (int t = 0; t < 32; t += 2) {
-    const uint64_t x2 = ffma2(f2pack(__uint_as_float(r[t]), __uint_as_float(r[t + 1])), scale2, negm2);
-    float e0, e1;
-    if (((t >> 1) & kPolyMask) == kPolyMask) {
-      ex2_poly2(x2, e0, e1);
-    } else {
-      float x0, x1;
-      f2unpack(x2, x0, x1);
-      e0 = ex2(x0);
-      e1 = ex2(x1);
-    }
-    if constexpr (!FULL) {
-      if (kbase + t >= limit) e0 = 0.f;
-      if (kbase + t + 1 >= limit) e1 = 0.f;
-    }
-    r[t] = __float_as_uint(e0);
-    r[t + 1] = __float_as_uint(e1);
-    pk[t / 2] = pack_half2(e0, e1);
-  }
-}
-
-// bounded wait whose result is the same in every lane, so the warp-collective tcgen05.ld / st that
-// follow are reached by all lanes or by none
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, status, code));
-}
 
 __global__ void __launch_bounds__(ATT_THREADS, 1)
     attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -573,6 +436,22 @@ cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s) {
   if (!a.q || !a.k || !a.v || !a.o || a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return cudaErrorInvalidValue;
   if ((a.ldq | a.ldk | a.ldv | a.ldo | a.q_col0 | a.k_col0 | a.v_col0) & 7) return cudaErrorInvalidValue;
   if (!(a.scale > 0.f)) return cudaErrorInvalidValue;  // the row max is taken on unscaled scores
+  // at most 256 keys (the cross-attention over the context) and at most six 128-query tiles per SM: the
+  // short-key kernel (attn_short.cu: K and V resident, Q tiles streamed, one exact softmax step), which
+  // gets a CTA's few tiles done sooner (Anima cross-attention, 1 / 2 / 4 images: 11.9 -> 10.5, 17.6 -> 15.0,
+  // 24.1 -> 23.7 us). With more tiles per SM its per-tile chain (S, softmax over 256 keys, P V, O read out
+  // before the slot's next S) is longer than the general kernel's pipeline: 8 images 43 us against 49.
+  // HX_ATTN_SHORT=0 / 1 in the environment: never / always for 128 < Tk <= 256.
+  static const int short_mode = [] {
+    const char* e = getenv("HX_ATTN_SHORT");
+    return e && *e ? atoi(e) : -1;
+  }();
+  if (a.kernel == 0 && a.Tk > KT && a.Tk <= 2 * KT && short_mode != 0) {
+    const long long units = static_cast<long long>((a.Tq + QT - 1) / QT) * a.H * a.B;
+    if (short_mode == 1 || units <= 6LL * sm_count()) return attn_short_launch(a, s);
+  }
+  if (a.kernel == 2) return attn_short_launch(a, s);
+  if (a.kernel != 0 && a.kernel != 1) return cudaErrorInvalidValue;
   CUtensorMap tQ, tK, tV;
   const uint64_t qp = static_cast<uint64_t>(a.ldq) * 2, kp = static_cast<uint64_t>(a.ldk) * 2,
                  vp = static_cast<uint64_t>(a.ldv) * 2;

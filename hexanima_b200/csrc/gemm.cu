@@ -131,15 +131,17 @@ struct Sched {
 
 // ---------------------------------------------------------------- dequantisers
 // One k-block (64 k) of a 256-row weight tile: raw smem -> fp16 SW128 K-major smem.
-// ROWS weight rows per k-block (256 for the 1-CTA tile, 128 per CTA of a pair); 256 dequant threads.
+// ROWS weight rows per k-block (256 for the 1-CTA tile, 128 or 112 per CTA of a pair); 256 dequant threads.
+// A last, partial pass (ROWS = 112) is skipped by whole warps (8 rows per warp for q8, 16 for q4).
 template <int FMT, int ROWS = BN>
 __device__ __forceinline__ void dequant_kblock(uint32_t raw, uint32_t dq, const __half* sc, int group, int dt) {
   if constexpr (FMT == WF_Q8) {
     const int c = dt & 3, r0 = dt >> 2;
     const __half2 off = __half2half2(__ushort_as_half(0x6480));  // 1152.0
 #pragma unroll
-    for (int pass = 0; pass < ROWS / 64; ++pass) {
+    for (int pass = 0; pass < (ROWS + 63) / 64; ++pass) {
       const int n = pass * 64 + r0;
+      if (ROWS % 64 != 0 && n >= ROWS) break;
       const uint4 v = ld_shared_v4(raw + n * 64 + c * 16);
       const __half s = group == 64 ? sc[n] : sc[(c >> 1) * ROWS + n];
       const __half2 s2 = __half2half2(s);
@@ -162,8 +164,9 @@ __device__ __forceinline__ void dequant_kblock(uint32_t raw, uint32_t dq, const 
     // q4 / q4a: 32 raw bytes per row, two threads per row, each thread one 32-k group
     const int c = dt & 1, r0 = dt >> 1;
 #pragma unroll
-    for (int pass = 0; pass < ROWS / 128; ++pass) {
+    for (int pass = 0; pass < (ROWS + 127) / 128; ++pass) {
       const int n = pass * 128 + r0;
+      if (ROWS % 128 != 0 && n >= ROWS) break;
       const uint4 v = ld_shared_v4(raw + n * 32 + c * 16);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
       const __half s = sc[c * ROWS + n];
@@ -215,9 +218,12 @@ __device__ __forceinline__ float situ(float h, float g) {
   return (4.0f * tanhf(g * 0.25f) * (1.0f / (1.0f + expf(-g)))) * (25.0f * tanhf(h * 0.04f));
 }
 
-template <int EPI>
+// TN: the tile's accumulator columns (256, or 224 for the CTA-pair GELU / store tiles that fill the
+// waves of an N = 8192 GEMM better)
+template <int EPI, int TN = BN>
 __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, int m0, int n0, int warp, int lane,
                                               const CUtensorMap* tmX, uint8_t* stage_ptr) {
+  static_assert(TN == BN || ((EPI == EPI_GELU || EPI == EPI_STORE) && TN % 32 == 0), "tile width");
   const int m = m0 + warp * 32 + lane;
   const bool row_ok = m < p.M;
   const uint32_t tl = tacc + (static_cast<uint32_t>(warp * 32) << 16);
@@ -229,7 +235,7 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
   float v[32];
   if constexpr (EPI == EPI_STORE32) {
 #pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
+    for (int c = 0; c < TN / 32; ++c) {
       const int n = n0 + 32 * c;
       if (n >= p.N) break;
       tmem_ld32(tl + 32 * c, r);
@@ -243,11 +249,23 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, uint32_t tacc, i
     }
   } else if constexpr (EPI == EPI_STORE || EPI == EPI_GELU) {
     // fp16 out: 64 columns at a time staged in the 128-B swizzled stage, written by one TMA store
-    // (the tensor map clips rows >= M and columns >= N)
+    // (the tensor map clips rows >= M and columns >= N); a last 32 columns (TN = 224) by plain row stores,
+    // since a 64-column box would overwrite the next tile's first columns
     const int row = warp * 32 + lane;
 #pragma unroll 1
-    for (int g = 0; g < BN / 64; ++g) {
+    for (int g = 0; g < (TN + 63) / 64; ++g) {
       if (n0 + 64 * g >= p.N) break;  // uniform over the epilogue warps
+      if (TN % 64 != 0 && g == TN / 64) {
+        tmem_ld32(tl + 64 * g, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+        if constexpr (EPI == EPI_GELU) {
+          gelu32(v);
+        }
+        if (row_ok) store_row32_f16(p.out + static_cast<size_t>(m) * p.ldo + n0 + 64 * g, v);
+        break;
+      }
       if (threadIdx.x == 0) bulk_wait_read<0>();  // the previous group's store has read the stage
       named_bar(1, EPI_WARPS * 32);
 #pragma unroll 1
@@ -688,16 +706,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 //   tfull   (each)  : accumulator ready, commit multicast; tempty (leader): 4 epilogue warps per CTA
 constexpr int HALF = 128;
 
-template <int FMT>
+// TN: the pair tile's N (256, or 224: each CTA then holds 112 weight rows of the B operand). Every stage
+// part stays a multiple of 1 KB, the alignment of the 128-byte swizzled operand tiles.
+template <int FMT, int TN = BN>
 struct Cfg2 {
+  static constexpr int HB = TN / 2;  // weight rows per CTA
   static constexpr int A_B = HALF * BK * 2;
-  static constexpr int WDQ_B = HALF * BK * 2;
-  static constexpr int RAW_B = FMT == WF_F16 ? 0 : FMT == WF_Q8 ? HALF * BK : HALF * BK / 2;
+  static constexpr int WDQ_B = HB * BK * 2;
+  static constexpr int RAW_B = FMT == WF_F16 ? 0 : FMT == WF_Q8 ? HB * BK : HB * BK / 2;
   static constexpr int SC_B = FMT == WF_F16 ? 0 : 1024;
   static constexpr int STAGE = A_B + WDQ_B + RAW_B + SC_B;
   static constexpr int STAGES = FMT == WF_F16 ? 6 : 5;
   static constexpr int OUT_STAGE = 16384;
   static constexpr int SMEM = STAGES * STAGE + OUT_STAGE + 1024 + 1024;
+  static_assert(WDQ_B % 1024 == 0 && RAW_B % 1024 == 0 && STAGE % 1024 == 0, "stage alignment");
+  static_assert(TN == BN || TN == 224, "pair tile width");
 };
 
 __device__ __forceinline__ void spin_ns(uint64_t ns) {
@@ -706,13 +729,14 @@ __device__ __forceinline__ void spin_ns(uint64_t ns) {
   }
 }
 
-template <int FMT, int EPI>
+template <int FMT, int EPI, int TN = BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                  const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmS,
                  const __grid_constant__ CUtensorMap tmMin, const __grid_constant__ CUtensorMap tmX,
                  const KParams p) {
-  using C = Cfg2<FMT>;
+  using C = Cfg2<FMT, TN>;
+  constexpr int HB = C::HB;
   constexpr int S = C::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -765,7 +789,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_base_slot;
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int row0 = static_cast<int>(rank) * HALF;
+  const int row0 = static_cast<int>(rank) * HALF;  // this CTA's A rows in the pair tile
+  const int brow0 = static_cast<int>(rank) * HB;   // and its weight rows
   // Quantised weight tiles and scales are constant during inference (no kernel that can precede this one
   // with programmatic dependent launch writes them; fp16 weights can be an expansion just before, so they
   // wait), so the producer loads the first ring of them before waiting for the previous kernel.
@@ -776,8 +801,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int t, kb0, kb1;
       if (sched.next(p, t, kb0, kb1)) {
         const uint32_t sc_rows = BK / p.group;
-        const uint32_t raw_tx = C::RAW_B + sc_rows * HALF * 2 * (FMT == WF_Q4A ? 2 : 1);
-        const int n0 = tile_n(p, t) * BN + row0;
+        const uint32_t raw_tx = C::RAW_B + sc_rows * HB * 2 * (FMT == WF_Q4A ? 2 : 1);
+        const int n0 = tile_n(p, t) * TN + brow0;
         npre = kb1 - kb0 < S ? kb1 - kb0 : S;
         for (int i = 0; i < npre; ++i) {  // stages i are empty on the first pass
           const int kb = kb0 + i;
@@ -785,7 +810,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           tma_load_2d(st_raw(i), &tmW, &raw_full[i], FMT == WF_Q8 ? kb * BK : kb * (BK / 2), n0);
           tma_load_2d(st_sc(i), &tmS, &raw_full[i], n0, kb * static_cast<int>(sc_rows));
           if constexpr (FMT == WF_Q4A)
-            tma_load_2d(st_sc(i) + 2 * HALF * 2, &tmMin, &raw_full[i], n0, kb * static_cast<int>(sc_rows));
+            tma_load_2d(st_sc(i) + 2 * HB * 2, &tmMin, &raw_full[i], n0, kb * static_cast<int>(sc_rows));
         }
       }
     }
@@ -797,13 +822,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       const uint32_t tx_a = 2u * (C::A_B + (FMT == WF_F16 ? C::WDQ_B : 0));
       const uint32_t sc_rows = FMT == WF_F16 ? 0 : (BK / p.group);
-      const uint32_t raw_tx = C::RAW_B + sc_rows * HALF * 2 * (FMT == WF_Q4A ? 2 : 1);
+      const uint32_t raw_tx = C::RAW_B + sc_rows * HB * 2 * (FMT == WF_Q4A ? 2 : 1);
       int it = 0;
       bool ok = true;
       Sched sched(p, pair, npairs);
       int t, kb0, kb1;
       while (ok && sched.next(p, t, kb0, kb1)) {
-        const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * BN + row0;
+        const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * TN + brow0;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -818,7 +843,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             tma_load_2d(st_raw(s), &tmW, &raw_full[s], FMT == WF_Q8 ? kb * BK : kb * (BK / 2), n0);
             tma_load_2d(st_sc(s), &tmS, &raw_full[s], n0, kb * static_cast<int>(sc_rows));
             if constexpr (FMT == WF_Q4A)
-              tma_load_2d(st_sc(s) + 2 * HALF * 2, &tmMin, &raw_full[s], n0, kb * static_cast<int>(sc_rows));
+              tma_load_2d(st_sc(s) + 2 * HB * 2, &tmMin, &raw_full[s], n0, kb * static_cast<int>(sc_rows));
           }
         }
       }
@@ -826,7 +851,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp == MMA_WARP) {
     if (lane == 0 && leader) {
-      constexpr uint32_t idesc = idesc_f16(2 * HALF, BN, 0, 0);
+      constexpr uint32_t idesc = idesc_f16(2 * HALF, TN, 0, 0);
       int it = 0;
       bool ok = true, issued = false;
       Sched sched(p, pair, npairs);
@@ -835,7 +860,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const int acc = ti & 1;
         if (!mbar_wait(&tempty[acc], ((ti >> 1) & 1) ^ 1, p.status, 112)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t dt = tmem + acc * BN;
+        const uint32_t dt = tmem + acc * BN;  // accumulators at columns 0 and 256 (TN <= 256 each)
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
@@ -872,7 +897,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int s = it % S;
           const uint32_t ph = (it / S) & 1;
           if (!mbar_wait(&raw_full[s], ph, p.status, 115)) { ok = false; break; }
-          dequant_kblock<FMT, HALF>(smem_u32(st_raw(s)), smem_u32(st_w(s)), reinterpret_cast<const __half*>(st_sc(s)),
+          dequant_kblock<FMT, HB>(smem_u32(st_raw(s)), smem_u32(st_w(s)), reinterpret_cast<const __half*>(st_sc(s)),
                                     p.group, dt);
           fence_proxy_async_smem();
           __syncwarp();
@@ -885,11 +910,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     Sched sched(p, pair, npairs);
     int t, kb0, kb1;
     for (int ti = 0; ok && sched.next(p, t, kb0, kb1); ++ti) {
-      const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * BN;
+      const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * TN;
       const int acc = ti & 1;
       if (!mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 116)) { ok = false; break; }
       tc_fence_after();
-      epilogue_tile<EPI>(p, tmem + acc * BN, m0, n0, warp, lane, &tmX, out_stage);
+      epilogue_tile<EPI, TN>(p, tmem + acc * BN, m0, n0, warp, lane, &tmX, out_stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_leader(&tempty[acc]);
@@ -968,6 +993,14 @@ int group_m_override() {
   return g;
 }
 
+int pair_tn_override() {
+  static const int t = [] {
+    const char* e = getenv("HX_PAIR_TN");
+    return e && *e ? atoi(e) : 0;
+  }();
+  return t;
+}
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* e = getenv("HX_PDL");
@@ -1006,16 +1039,16 @@ static cudaError_t launch_t(const GemmArgs& a, const KParams& p, const CUtensorM
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-template <int FMT, int EPI>
+template <int FMT, int EPI, int TN = BN>
 static cudaError_t launch_pair_t(const GemmArgs& a, const KParams& p, const CUtensorMap& tA, const CUtensorMap& tA2,
                                  const CUtensorMap& tW, const CUtensorMap& tS, const CUtensorMap& tMin,
                                  const CUtensorMap& tX, cudaStream_t s) {
-  using C = Cfg2<FMT>;
+  using C = Cfg2<FMT, TN>;
   static uint64_t attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_set >> dev & 1)) {
-    cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(gemm2_kernel<FMT, EPI, TN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     attr_set |= 1ull << dev;
   }
@@ -1035,13 +1068,21 @@ static cudaError_t launch_pair_t(const GemmArgs& a, const KParams& p, const CUte
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_attr(attr, 1);
-  return cudaLaunchKernelEx(&cfg, gemm2_kernel<FMT, EPI>, tA, tA2, tW, tS, tMin, tX, p);
+  return cudaLaunchKernelEx(&cfg, gemm2_kernel<FMT, EPI, TN>, tA, tA2, tW, tS, tMin, tX, p);
 }
 
 template <int FMT>
 static cudaError_t launch_pair_fmt(const GemmArgs& a, const KParams& p, const CUtensorMap& tA, const CUtensorMap& tA2,
                                    const CUtensorMap& tW, const CUtensorMap& tS, const CUtensorMap& tMin,
-                                   const CUtensorMap& tX, cudaStream_t s) {
+                                   const CUtensorMap& tX, cudaStream_t s, int tn) {
+  if constexpr (FMT == WF_F16 || FMT == WF_Q8) {
+    if (tn == 224) {
+      if (a.epi == EPI_GELU) return launch_pair_t<FMT, EPI_GELU, 224>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+      if (a.epi == EPI_STORE) return launch_pair_t<FMT, EPI_STORE, 224>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+      return cudaErrorInvalidValue;
+    }
+  }
+  if (tn != BN) return cudaErrorInvalidValue;
   switch (a.epi) {
     case EPI_STORE: return launch_pair_t<FMT, EPI_STORE>(a, p, tA, tA2, tW, tS, tMin, tX, s);
     case EPI_RESID: return launch_pair_t<FMT, EPI_RESID>(a, p, tA, tA2, tW, tS, tMin, tX, s);
@@ -1153,7 +1194,34 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
     pair = true;
     streamk = 1;
   }
-  const uint32_t wrows = pair ? HALF : BN;
+  // CTA-pair GELU tiles 224 columns wide when they take no more waves than 256-column tiles: N = 8192
+  // makes 32 tiles of 256 per 256-row band but 37 of 224 (the last 128 wide), so at 1536 rows 222 tiles
+  // are exactly 3 waves on 74 pairs, as are 192 tiles of 256 (the last wave 60 % full), and at 3072 rows
+  // 444 against 384 tiles both take 6. A 224-column tile costs about 0.955 of a 256-column one (the A
+  // tile is loaded whole either way), so measured mlp.layer1: one image 54.0 -> 53.2 us (q8 in the main
+  // loop), 45.0 -> 43.7 (fp16), two images 92.8 -> 92.3; at four images (12 against 11 waves) 224 was
+  // slower (175.5 against 168.1) and is not taken. tile 5 forces 224 (GELU or plain store),
+  // HX_PAIR_TN=256 / 224 in the environment overrides the choice.
+  int tn = BN;
+  if (a.tile == 5) {
+    if ((a.epi != EPI_GELU && a.epi != EPI_STORE) || (W->fmt != WF_F16 && W->fmt != WF_Q8))
+      return cudaErrorInvalidValue;
+    pair = true;
+    tn = 224;
+  } else if (pair && !streamk && a.epi == EPI_GELU && (W->fmt == WF_F16 || W->fmt == WF_Q8)) {
+    const int ov = pair_tn_override();
+    if (ov == 224) {
+      tn = 224;
+    } else if (ov != BN) {
+      int np = sm_count() / 2;
+      if (a.max_ctas > 0 && a.max_ctas / 2 < np) np = a.max_ctas / 2 > 0 ? a.max_ctas / 2 : 1;
+      const long long mt = (a.M + 2 * HALF - 1) / (2 * HALF);
+      const long long w256 = (mt * ((N + BN - 1) / BN) + np - 1) / np;
+      const long long w224 = (mt * ((N + 223) / 224) + np - 1) / np;
+      if (w224 <= w256) tn = 224;
+    }
+  }
+  const uint32_t wrows = pair ? static_cast<uint32_t>(tn / 2) : BN;
 
   CUtensorMap tA, tA2, tW, tS, tMin, tX;
   memset(&tA2, 0, sizeof tA2);
@@ -1202,7 +1270,7 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   p.nkb1 = a.K1 / BK;
   p.group = W->fmt == WF_F16 ? 64 : W->group;
   p.num_m_tiles = pair ? (a.M + 2 * HALF - 1) / (2 * HALF) : (a.M + BM - 1) / BM;
-  p.num_n_tiles = (N + BN - 1) / BN;
+  p.num_n_tiles = (N + tn - 1) / tn;
   p.streamk = streamk;
   p.num_tiles = p.num_m_tiles * p.num_n_tiles;
   // default order walks M tiles under one weight block (the weight block stays in L2); when the A
@@ -1241,10 +1309,10 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
 
   if (pair) {
     switch (W->fmt) {
-      case WF_F16: return launch_pair_fmt<WF_F16>(a, p, tA, tA2, tW, tS, tMin, tX, s);
-      case WF_Q8: return launch_pair_fmt<WF_Q8>(a, p, tA, tA2, tW, tS, tMin, tX, s);
-      case WF_Q4: return launch_pair_fmt<WF_Q4>(a, p, tA, tA2, tW, tS, tMin, tX, s);
-      case WF_Q4A: return launch_pair_fmt<WF_Q4A>(a, p, tA, tA2, tW, tS, tMin, tX, s);
+      case WF_F16: return launch_pair_fmt<WF_F16>(a, p, tA, tA2, tW, tS, tMin, tX, s, tn);
+      case WF_Q8: return launch_pair_fmt<WF_Q8>(a, p, tA, tA2, tW, tS, tMin, tX, s, tn);
+      case WF_Q4: return launch_pair_fmt<WF_Q4>(a, p, tA, tA2, tW, tS, tMin, tX, s, tn);
+      case WF_Q4A: return launch_pair_fmt<WF_Q4A>(a, p, tA, tA2, tW, tS, tMin, tX, s, tn);
     }
     return cudaErrorInvalidValue;
   }

@@ -59,7 +59,8 @@ struct GemmArgs {
   int* status = nullptr;
   int max_ctas = 0;  // 0 = one CTA per SM
   // 0 auto, 1 single-CTA 128x256 tiles, 2 CTA-pair 256x256 tiles, 3 q8 weights in TMEM, 4 quantised
-  // weights expanded to fp16 in wexp first (auto does so from expand_min_rows() rows up)
+  // weights expanded to fp16 in wexp first (auto does so from expand_min_rows() rows up), 5 CTA-pair
+  // 256x224 tiles (GELU or store epilogue, fp16 or q8 weights)
   int tile = 0;
   // scratch for the expanded weights (fp16 [N][K]); nullptr or too small: dequantise inside the GEMM
   __half* wexp = nullptr;
@@ -80,9 +81,13 @@ struct AttnArgs {
   int nvalid = 0;       // keys with index >= nvalid get probability 0 (0 = all Tk keys valid)
   float scale = 1.0f;   // logits are q.k * scale
   int* status = nullptr;
+  // 0 auto (the short-key kernel for 128 < Tk <= 256 with at most six 128-query tiles per SM), 1 the general
+  // online-softmax kernel, 2 the short-key kernel (Tk <= 256)
+  int kernel = 0;
 };
 
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s);
+cudaError_t attn_short_launch(const AttnArgs& a, cudaStream_t s);
 // q8 GEMM with the dequantised weights in TMEM (gemm_wt.cu): STORE / GELU / RESID / RMS epilogues,
 // N a multiple of 256; gemm_launch picks it for the RMS epilogue when its tiles fill the GPU (tile 3
 // forces it)

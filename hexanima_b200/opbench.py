@@ -25,7 +25,8 @@ def main(argv=None):
     ap.add_argument("--ops", default="all")
     ap.add_argument("--fmt", choices=["q8", "f16", "q4"], default="q8")
     ap.add_argument("--json", action="store_true")
-    ap.add_argument("--tile", type=int, default=0, help="GEMM tiles: 0 auto, 1 single-CTA, 2 CTA pair, 3 q8 weights in TMEM")
+    ap.add_argument("--tile", type=int, default=0, help="GEMM tiles: 0 auto, 1 single-CTA, 2 CTA pair, 3 q8 weights in TMEM, "
+                    "4 expanded to fp16 first, 5 CTA pair 256x224 (GELU / store only)")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
     h = rt.Handle(0)

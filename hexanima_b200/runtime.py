@@ -114,7 +114,8 @@ class hx_attn_desc(ctypes.Structure):
                 ("k", ctypes.c_void_p), ("ldk", ctypes.c_int), ("k_col0", ctypes.c_int),
                 ("v", ctypes.c_void_p), ("ldv", ctypes.c_int), ("v_col0", ctypes.c_int),
                 ("o", ctypes.c_void_p), ("ldo", ctypes.c_int), ("batch", ctypes.c_int), ("heads", ctypes.c_int),
-                ("tq", ctypes.c_int), ("tk", ctypes.c_int), ("nvalid", ctypes.c_int), ("scale", ctypes.c_float)]
+                ("tq", ctypes.c_int), ("tk", ctypes.c_int), ("nvalid", ctypes.c_int), ("scale", ctypes.c_float),
+                ("kernel", ctypes.c_int)]
 
 
 _lib = None
@@ -463,9 +464,9 @@ class Handle:
         _check(lib().hx_gemm(self.h, ctypes.byref(d)), "hx_gemm")
 
     def attention(self, q, k, v, o, batch, heads, tq, tk, ldq, ldk, ldv, ldo, q_col0=0, k_col0=0, v_col0=0,
-                  nvalid=0, scale=1.0):
+                  nvalid=0, scale=1.0, kernel=0):
         d = hx_attn_desc(_ptr(q), ldq, q_col0, _ptr(k), ldk, k_col0, _ptr(v), ldv, v_col0, _ptr(o), ldo, batch,
-                         heads, tq, tk, nvalid, scale)
+                         heads, tq, tk, nvalid, scale, kernel)
         _check(lib().hx_attention(self.h, ctypes.byref(d)), "hx_attention")
 
     def lnmod(self, x, h16, rows, D, shift, scale, vec_bstride=0, rows_per_img=0, eps=1e-6):

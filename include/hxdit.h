@@ -389,7 +389,10 @@ typedef struct {
   float eps;
   int tile;                     /* 0 auto, 1 single-CTA 128x256, 2 CTA-pair 256x256, 3 q8 weights in TMEM,
                                    4 quantised weights expanded to fp16 in the handle's scratch first (auto
-                                   does so from 3072 rows up; HX_EXPAND_ROWS in the environment overrides) */
+                                   does so from 3072 rows up; HX_EXPAND_ROWS in the environment overrides),
+                                   5 CTA-pair 256x224 (HX_EPI_GELU or HX_EPI_STORE, fp16 or q8 weights;
+                                   auto picks it for GELU when it needs fewer waves, HX_PAIR_TN=256 / 224
+                                   overrides) */
 } hx_gemm_desc;
 #define HX_EPI_STORE 0
 #define HX_EPI_RESID 1
@@ -407,6 +410,10 @@ typedef struct {
   void* o; int ldo;
   int batch, heads, tq, tk, nvalid;
   float scale;
+  int kernel;                   /* 0 auto, 1 the general kernel (online softmax over 128-key tiles), 2 the
+                                   short-key kernel (tk <= 256: K and V resident, one exact softmax step;
+                                   auto takes it for 128 < tk <= 256 with at most six 128-query tiles per
+                                   SM; HX_ATTN_SHORT=0 / 1: never / always) */
 } hx_attn_desc;
 /* softmax(q k^T * scale) v per head, head_dim 128: attn_run (hexagon/mega/blk.c:54-91,
  * masked moss/hexagon/mega/blk.c:54-94). Keys >= nvalid are masked (0 = none). */

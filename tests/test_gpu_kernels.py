@@ -26,6 +26,7 @@ def h():
 
 TILES = [1, 2]  # single-CTA 128x256 tiles, CTA-pair 256x256 tiles (cta_group::2)
 TILES3 = [1, 2, 3, 4]  # + q8 weights dequantised into TMEM; quantised weights expanded to fp16 first
+TILE224 = 5  # CTA-pair 256x224 tiles (112 weight rows per CTA): GELU / store epilogues, fp16 or q8 weights
 
 
 def _onehot_dequant(h, fmt, w, group, tile):
@@ -39,12 +40,14 @@ def _onehot_dequant(h, fmt, w, group, tile):
     return out.cpu().T.contiguous(), deq
 
 
-@pytest.mark.parametrize("tile", TILES3)
+@pytest.mark.parametrize("tile", TILES3 + [TILE224])
 @pytest.mark.parametrize("fmt,group", [(rt.FMT_F16, 64), (rt.FMT_Q8, 32), (rt.FMT_Q8, 64), (rt.FMT_Q4, 32),
                                        (rt.FMT_Q4A, 32)])
 def test_dequant_bit_exact(h, fmt, group, tile):
     if tile == 3 and fmt != rt.FMT_Q8:
         pytest.skip("the TMEM-weight kernel takes q8 weights")
+    if tile == TILE224 and fmt not in (rt.FMT_F16, rt.FMT_Q8):
+        pytest.skip("224-column pair tiles take fp16 or q8 weights")
     rng = np.random.default_rng(7)
     N, K = (512 if tile == 3 else 320), 256
     w = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
@@ -60,11 +63,13 @@ def _ref_gemm(A16, Wd):
     return A16.float().cpu() @ Wd.T
 
 
-@pytest.mark.parametrize("tile", TILES3)
+@pytest.mark.parametrize("tile", TILES3 + [TILE224])
 @pytest.mark.parametrize("fmt", [rt.FMT_F16, rt.FMT_Q8, rt.FMT_Q4])
 def test_gemm_store_and_gelu(h, fmt, tile):
     if tile == 3 and fmt != rt.FMT_Q8:
         pytest.skip("the TMEM-weight kernel takes q8 weights")
+    if tile == TILE224 and fmt == rt.FMT_Q4:
+        pytest.skip("224-column pair tiles take fp16 or q8 weights")
     torch.manual_seed(1)
     M, K, N = 300, 512, (512 if tile == 3 else 544)
     A = torch.randn(M, K).half()
@@ -72,7 +77,9 @@ def test_gemm_store_and_gelu(h, fmt, tile):
     ref = _ref_gemm(A, Wd)
     for epi, f in ((rt.EPI_STORE, lambda t: t), (rt.EPI_GELU, oa.gelu)):
         out = torch.zeros(M, N, dtype=torch.float16, device="cuda")
-        h.gemm(A.cuda(), M, mat, epi, lda=K, out=out, ldo=N, tile=tile)
+        Ad = A.cuda()
+        torch.cuda.synchronize()  # torch's stream and the handle's (non-blocking) stream are not ordered
+        h.gemm(Ad, M, mat, epi, lda=K, out=out, ldo=N, tile=tile)
         h.sync()
         assert rel(out.float(), f(ref)) < 2e-3
 
@@ -219,11 +226,10 @@ def test_expanded_weights_same_bits(h, fmt, group):
     A = (torch.randn(M, K1, device="cuda") * 0.5).half()
     L = torch.randn(M, 128, device="cuda").half()
     mat, keep, Wd = make_mat(fmt, (torch.randn(N, K1 + 128) * 0.05).numpy(), group)
-    outs = []
-    for tile in (2, 0, 4):
-        o = torch.zeros(M, N, dtype=torch.float16, device="cuda")
+    outs = [torch.zeros(M, N, dtype=torch.float16, device="cuda") for _ in range(3)]
+    torch.cuda.synchronize()  # the fills (torch's stream) complete before the handle's stream writes
+    for tile, o in zip((2, 0, 4), outs):
         h.gemm(A, M, mat, rt.EPI_STORE, lda=K1, k1=K1, a2=L.data_ptr(), lda2=128, out=o, ldo=N, tile=tile)
-        outs.append(o)
     h.sync()
     ref = torch.cat((A.float().cpu(), L.float().cpu()), 1) @ Wd.T
     assert rel(outs[0].float().cpu(), ref) < 2e-3
@@ -248,6 +254,32 @@ def test_gemm_pair_tiles_large(h, fmt):
     assert rel(o1.float(), o2.float()) < 1e-3
 
 
+@pytest.mark.parametrize("fmt,group,M,N", [(rt.FMT_F16, 64, 1536, 8192), (rt.FMT_Q8, 64, 1536, 8192),
+                                           (rt.FMT_Q8, 32, 1536, 8192), (rt.FMT_Q8, 64, 3072, 8192),
+                                           (rt.FMT_F16, 64, 600, 1024), (rt.FMT_Q8, 32, 600, 1024)])
+def test_gemm_pair_224_tiles(h, fmt, group, M, N):
+    """256x224 pair tiles (tile 5, and the automatic choice for mlp.layer1 at one and two images) against
+    fp32 math on the same operands and against the 256x256 pair tiles: the accumulation order over K is the
+    same, so the outputs agree to fp16 rounding of equal sums. N = 8192 makes 37 tiles per band, the last
+    128 wide; N = 1024 makes 5, the last 128 wide. At 3072 rows the automatic choice expands the q8 weights
+    and runs the fp16 kernel with 224-column tiles."""
+    torch.manual_seed(21)
+    K = 2048 if M >= 1536 else 512
+    A = torch.randn(M, K, device="cuda").half()
+    mat, keep, Wd = make_mat(fmt, (torch.randn(N, K) * 0.03).numpy(), group)
+    outs = {t: torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda") for t in (TILE224, 2, 0)}
+    torch.cuda.synchronize()  # the NaN fills (torch's stream) complete before the handle's stream writes
+    for tile, o in outs.items():
+        h.gemm(A, M, mat, rt.EPI_GELU, lda=K, out=o, ldo=N, tile=tile)
+    h.sync()
+    ref = oa.gelu(A.float().cpu() @ Wd.T)
+    for tile, o in outs.items():
+        oc = o.float().cpu()
+        assert torch.isfinite(oc).all(), tile
+        assert rel(oc, ref) < 2e-3, tile
+    assert rel(outs[TILE224].float(), outs[2].float()) < 1e-3
+
+
 @pytest.mark.parametrize("B,H,Tq,Tk,nvalid,amp", [(2, 2, 200, 333, 300, 0.6), (1, 3, 256, 256, 0, 0.6),
                                                    (2, 16, 1536, 1536, 0, 0.6), (1, 2, 130, 70, 0, 0.6),
                                                    (1, 2, 256, 520, 70, 2.5), (1, 4, 384, 1024, 0, 2.5)])
@@ -270,6 +302,37 @@ def test_attention(h, B, H, Tq, Tk, nvalid, amp):
     v = kv[..., D:].float().view(B, Tk, H, 128)
     ref = oa.attention(q, k, v, scale=scale, nvalid=nvalid or None).reshape(B, Tq, D)
     assert rel(out.float(), ref) < 2e-3
+
+
+@pytest.mark.parametrize("B,H,Tq,Tk,nvalid,amp", [(8, 16, 1536, 256, 0, 0.6), (1, 16, 1536, 256, 0, 2.5),
+                                                   (2, 3, 200, 256, 250, 0.6), (1, 2, 130, 70, 0, 2.5),
+                                                   (3, 5, 64, 200, 130, 0.6), (1, 1, 1000, 129, 0, 0.6)])
+def test_attention_short_keys(h, B, H, Tq, Tk, nvalid, amp):
+    """The short-key kernel (kernel 2: at most 256 keys, K and V resident per (image, head), one exact
+    softmax step) against the fp32 reference and against the general kernel (kernel 1) on the same inputs:
+    the Anima cross-attention at 8 and 1 images (T 1536, C 256), partial query tiles, masked keys (nvalid),
+    fewer than 128 keys, and CTAs whose query-tile range spans several (image, head) groups."""
+    torch.manual_seed(16)
+    D = 128 * H
+    qbuf = (torch.randn(B, Tq, 3 * D) * amp).half()
+    kv = (torch.randn(B, Tk, 2 * D) * amp).half()
+    outs = {kn: torch.full((B, Tq, D), float("nan"), dtype=torch.float16, device="cuda") for kn in (2, 1, 0)}
+    scale = 1.0 / math.sqrt(128)
+    qc, kvc = qbuf.cuda(), kv.cuda()
+    torch.cuda.synchronize()  # the fills and copies (torch's stream) complete before the handle's stream runs
+    for kn, o in outs.items():
+        h.attention(qc, kvc, kvc, o, B, H, Tq, Tk, 3 * D, 2 * D, 2 * D, D, q_col0=D, k_col0=0, v_col0=D,
+                    nvalid=nvalid, scale=scale, kernel=kn)
+    h.sync()
+    q = qbuf[..., D:2 * D].float().view(B, Tq, H, 128)
+    k = kv[..., :D].float().view(B, Tk, H, 128)
+    v = kv[..., D:].float().view(B, Tk, H, 128)
+    ref = oa.attention(q, k, v, scale=scale, nvalid=nvalid or None).reshape(B, Tq, D)
+    for kn, o in outs.items():
+        oc = o.float().cpu()
+        assert torch.isfinite(oc).all(), kn
+        assert rel(oc, ref) < 2e-3, kn
+    assert rel(outs[2].float(), outs[1].float()) < 2e-3
 
 
 @pytest.mark.parametrize("D", [1024, 2048, 3072])
@@ -297,3 +360,13 @@ def test_bad_arguments_are_rejected(h):
         h.gemm(A, 64, mat, rt.EPI_STORE, lda=100, out=out, ldo=64)
     with pytest.raises(rt.HxError):
         h.attention(A, A, A, out, 1, 1, 64, 64, 100, 100, 100, 64)  # row pitch not 16-byte aligned
+    m2, keep2, _ = make_mat(rt.FMT_F16, np.zeros((256, 128), np.float32))
+    A2 = torch.zeros(64, 128, dtype=torch.float16, device="cuda")
+    x = torch.zeros(64, 256, device="cuda")
+    g = torch.zeros(256, device="cuda")
+    q3 = torch.zeros(1, 128, 128, dtype=torch.float16, device="cuda")
+    kv3 = torch.zeros(1, 300, 128, dtype=torch.float16, device="cuda")
+    with pytest.raises(rt.HxError):  # the short-key kernel takes at most 256 keys
+        h.attention(q3, kv3, kv3, q3, 1, 1, 128, 300, 128, 128, 128, 128, scale=1.0, kernel=2)
+    with pytest.raises(rt.HxError):  # 224-column pair tiles take the GELU and store epilogues only
+        h.gemm(A2, 64, m2, rt.EPI_RESID, lda=128, x=x, ldx=256, gate=g, tile=5)
