@@ -248,11 +248,11 @@ def cpu_baseline_leg():
 
 
 # ---------------------------------------------------------------------------------------- GPU leg
-def time_q8_gemm(h, rt, torch, dev, M, iters=20):
+def time_q8_gemm(h, rt, torch, dev, M, iters=20, trials=3):
     """Live roofline leg: the dominant operation (mlp.layer1 GEMM with q8 weights, M x 8192 x 2048, GELU
-    epilogue) timed alone with CUDA events on the runtime's stream. From the library's expansion threshold
-    up (3072 rows) one call is two launches, the weight expansion to fp16 and the fp16 GEMM, and both
-    are inside the timed region."""
+    epilogue) timed alone with CUDA events on the runtime's stream: the median of `trials` runs of `iters`
+    back-to-back calls. From the library's expansion threshold up (3072 rows) one call is two launches,
+    the weight expansion to fp16 and the fp16 GEMM, and both are inside the timed region."""
     g = torch.Generator(device=dev).manual_seed(99)
     if FMT == "f16":
         u = (0.02 * torch.randn(F, D, device=dev, generator=g)).half()
@@ -267,13 +267,16 @@ def time_q8_gemm(h, rt, torch, dev, M, iters=20):
     for _ in range(3):
         h.gemm(A, M, mat, rt.EPI_GELU, lda=D, out=out, ldo=F)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    h.sync()
-    e0.record(stream)
-    for _ in range(iters):
-        h.gemm(A, M, mat, rt.EPI_GELU, lda=D, out=out, ldo=F)
-    e1.record(stream)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1) / iters
+    times = []
+    for _ in range(trials):
+        h.sync()
+        e0.record(stream)
+        for _ in range(iters):
+            h.gemm(A, M, mat, rt.EPI_GELU, lda=D, out=out, ldo=F)
+        e1.record(stream)
+        e1.synchronize()
+        times.append(e0.elapsed_time(e1) / iters)
+    ms = float(np.median(times))
     return 2.0 * M * F * D / (ms * 1e-3) / 1e12, ms
 
 
