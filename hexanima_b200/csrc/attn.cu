@@ -446,7 +446,8 @@ cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s) {
     const char* e = getenv("HX_ATTN_SHORT");
     return e && *e ? atoi(e) : -1;
   }();
-  if (a.kernel == 0 && a.Tk > KT && a.Tk <= 2 * KT && short_mode != 0) {
+  // (its O goes out by TMA stores: the output must start on a 16-byte boundary)
+  if (a.kernel == 0 && a.Tk > KT && a.Tk <= 2 * KT && short_mode != 0 && reinterpret_cast<uintptr_t>(a.o) % 16 == 0) {
     const long long units = static_cast<long long>((a.Tq + QT - 1) / QT) * a.H * a.B;
     if (short_mode == 1 || units <= 6LL * sm_count()) return attn_short_launch(a, s);
   }
