@@ -1,4 +1,4 @@
-"""The N>1 paths on CPU with world_size-2 gloo ranks.
+"""The N>1 paths on CPU with gloo ranks (world size 2, and 4 and 8 for the Ulysses layout).
 
 * Ulysses layout contract of hexanima_b200/csrc/sp.cu: pack q|k|v token shards into
   send[c][dst][T/P][D/P] (head group dst), all-to-all, attend over the full sequence on H/P heads,
@@ -51,12 +51,12 @@ def _sp_worker(rank, world, port, T, H, nvalid, out):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T,H,nvalid", [(64, 4, 64), (128, 6, 100)])
-def test_ulysses_exchange_layout_gloo(T, H, nvalid):
-    world = 2
+@pytest.mark.parametrize("world,T,H,nvalid", [(2, 64, 4, 64), (2, 128, 6, 100), (4, 128, 24, 120), (8, 256, 24, 250)])
+def test_ulysses_exchange_layout_gloo(world, T, H, nvalid):
+    """world 4 and 8 with the MOSS head count (24: 6 and 3 heads per rank), as the 4- and 8-GPU bench runs."""
     out = mp.get_context("spawn").Manager().dict()
     mp.spawn(_sp_worker, args=(world, _free_port(), T, H, nvalid, out), nprocs=world, join=True)
-    assert sorted(out.keys()) == [0, 1]
+    assert sorted(out.keys()) == list(range(world))
     assert max(out.values()) < 1e-5
 
 
