@@ -1,8 +1,8 @@
 """Generate the golden vectors that pin the oracle to the reference implementation.
 
-Run in a container that has the reference checkout (default /root/reference, override with
-HX_REFERENCE); the committed .npz files are what the tests read, so the reference is not needed
-to run the tests.
+Run in a container that has the reference checkout (its path in HX_REFERENCE, else the default
+below); the committed .npz files are what the tests read, so the reference is not needed to run the
+tests.
 
   python tests/golden/make_golden.py
 
