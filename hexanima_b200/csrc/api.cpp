@@ -2062,12 +2062,8 @@ int hx_moss_sample(hx_handle hh, int gfd, const int32_t* meta, int nmeta, const 
 }
 
 // ---------------------------------------------------------------- operator level
-int hx_gemm(hx_handle hh, const hx_gemm_desc* d) {
-  hx_ctx* h = H(hh);
-  if (!h || !d || !valid_mat(d->w)) return HX_E_ARG;
-  DevGuard g(h->device);
-  DevMat W = to_devmat(d->w);
-  GemmArgs a;
+// the operator descriptor as the launcher's arguments (W is the caller's copy of d->w)
+static void gemm_args_from_desc(const hx_gemm_desc* d, const DevMat& W, GemmArgs& a) {
   a.A = static_cast<const __half*>(d->a);
   a.lda = d->lda;
   a.A2 = static_cast<const __half*>(d->a2);
@@ -2093,6 +2089,15 @@ int hx_gemm(hx_handle hh, const hx_gemm_desc* d) {
   a.sinT = d->sin_t;
   a.eps = d->eps > 0.f ? d->eps : 1e-6f;
   a.tile = d->tile;
+}
+
+int hx_gemm(hx_handle hh, const hx_gemm_desc* d) {
+  hx_ctx* h = H(hh);
+  if (!h || !d || !valid_mat(d->w)) return HX_E_ARG;
+  DevGuard g(h->device);
+  DevMat W = to_devmat(d->w);
+  GemmArgs a;
+  gemm_args_from_desc(d, W, a);
   a.status = h->status;
   if (W.fmt != WF_F16 && (a.tile == 4 || (a.tile == 0 && a.M >= expand_min_rows())))
     reserve_wexp(h, static_cast<size_t>(W.N) * W.K * 2);
@@ -2102,11 +2107,36 @@ int hx_gemm(hx_handle hh, const hx_gemm_desc* d) {
   return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);
 }
 
-int hx_attention(hx_handle hh, const hx_attn_desc* d) {
-  hx_ctx* h = H(hh);
-  if (!h || !d) return HX_E_ARG;
-  DevGuard g(h->device);
-  AttnArgs a;
+int hx_gemm_query(const hx_gemm_desc* d, int sm_count, hx_gemm_plan* out) {
+  if (!d || !out || !valid_mat(d->w)) return HX_E_ARG;
+  DevMat W = to_devmat(d->w);
+  GemmArgs a;
+  gemm_args_from_desc(d, W, a);
+  GemmChoice c;
+  if (gemm_choose(a, sm_count, true, c) != cudaSuccess) return HX_E_ARG;
+  int expand = 0;
+  DevMat f;
+  if (c.expand) {  // the fp16 GEMM on the expanded weights (scratch of the handle, as hx_gemm reserves it)
+    expand = 1;
+    f.fmt = WF_F16;
+    f.N = W.N;
+    f.K = W.K;
+    f.group = 64;
+    f.w = W.w;
+    a.W = &f;
+    a.tile = 0;
+    if (gemm_choose(a, sm_count, false, c) != cudaSuccess) return HX_E_ARG;
+  }
+  out->kernel = c.kernel;
+  out->expand = expand;
+  out->tile_m = c.kernel == 1 ? 128 : 256;
+  out->tile_n = c.kernel == 2 ? c.tile_n : 256;
+  out->tiles = c.kernel == 3 ? gemm_wt_tiles(a) : c.tiles;
+  out->streamk = c.streamk;
+  return HX_OK;
+}
+
+static void attn_args_from_desc(const hx_attn_desc* d, AttnArgs& a) {
   a.q = static_cast<const __half*>(d->q);
   a.ldq = d->ldq;
   a.q_col0 = d->q_col0;
@@ -2125,9 +2155,27 @@ int hx_attention(hx_handle hh, const hx_attn_desc* d) {
   a.nvalid = d->nvalid;
   a.scale = d->scale;
   a.kernel = d->kernel;
+}
+
+int hx_attention(hx_handle hh, const hx_attn_desc* d) {
+  hx_ctx* h = H(hh);
+  if (!h || !d) return HX_E_ARG;
+  DevGuard g(h->device);
+  AttnArgs a;
+  attn_args_from_desc(d, a);
   a.status = h->status;
   cudaError_t e = attn_launch(a, h->stream);
   return e == cudaSuccess ? HX_OK : (e == cudaErrorInvalidValue ? HX_E_ARG : HX_E_CUDA);
+}
+
+int hx_attention_query(const hx_attn_desc* d, int sm_count, int32_t* kernel) {
+  if (!d || !kernel) return HX_E_ARG;
+  AttnArgs a;
+  attn_args_from_desc(d, a);
+  const int k = attn_choose(a, sm_count);
+  if (k < 0) return HX_E_ARG;
+  *kernel = k;
+  return HX_OK;
 }
 
 int hx_lnmod(hx_handle hh, const float* x, void* h16, int rows, int D, const float* shift, const float* scale,

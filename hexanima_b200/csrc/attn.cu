@@ -432,27 +432,36 @@ __global__ void __launch_bounds__(ATT_THREADS, 1)
 
 }  // namespace
 
-cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s) {
-  if (!a.q || !a.k || !a.v || !a.o || a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0) return cudaErrorInvalidValue;
-  if ((a.ldq | a.ldk | a.ldv | a.ldo | a.q_col0 | a.k_col0 | a.v_col0) & 7) return cudaErrorInvalidValue;
-  if (!(a.scale > 0.f)) return cudaErrorInvalidValue;  // the row max is taken on unscaled scores
+// which kernel attn_launch runs for these arguments on a GPU with `sms` SMs: 1 the general kernel, 2 the
+// short-key kernel, -1 invalid arguments (host-side; also answered by hx_attention_query)
+int attn_choose(const AttnArgs& a, int sms) {
+  if (!a.q || !a.k || !a.v || !a.o || a.B <= 0 || a.H <= 0 || a.Tq <= 0 || a.Tk <= 0 || sms < 1) return -1;
+  if ((a.ldq | a.ldk | a.ldv | a.ldo | a.q_col0 | a.k_col0 | a.v_col0) & 7) return -1;
+  if (!(a.scale > 0.f)) return -1;  // the row max is taken on unscaled scores
+  if (a.kernel == 2) return a.Tk <= 2 * KT ? 2 : -1;
+  if (a.kernel != 0 && a.kernel != 1) return -1;
   // at most 256 keys (the cross-attention over the context) and at most six 128-query tiles per SM: the
   // short-key kernel (attn_short.cu: K and V resident, Q tiles streamed, one exact softmax step), which
   // gets a CTA's few tiles done sooner (Anima cross-attention, 1 / 2 / 4 images: 11.9 -> 10.5, 17.6 -> 15.0,
   // 24.1 -> 23.7 us). With more tiles per SM its per-tile chain (S, softmax over 256 keys, P V, O read out
   // before the slot's next S) is longer than the general kernel's pipeline: 8 images 43 us against 49.
-  // HX_ATTN_SHORT=0 / 1 in the environment: never / always for 128 < Tk <= 256.
+  // HX_ATTN_SHORT=0 / 1 in the environment: never / always for 128 < Tk <= 256. Its O goes out by TMA
+  // stores, so the output must start on a 16-byte boundary.
   static const int short_mode = [] {
     const char* e = getenv("HX_ATTN_SHORT");
     return e && *e ? atoi(e) : -1;
   }();
-  // (its O goes out by TMA stores: the output must start on a 16-byte boundary)
   if (a.kernel == 0 && a.Tk > KT && a.Tk <= 2 * KT && short_mode != 0 && reinterpret_cast<uintptr_t>(a.o) % 16 == 0) {
     const long long units = static_cast<long long>((a.Tq + QT - 1) / QT) * a.H * a.B;
-    if (short_mode == 1 || units <= 6LL * sm_count()) return attn_short_launch(a, s);
+    if (short_mode == 1 || units <= 6LL * sms) return 2;
   }
-  if (a.kernel == 2) return attn_short_launch(a, s);
-  if (a.kernel != 0 && a.kernel != 1) return cudaErrorInvalidValue;
+  return 1;
+}
+
+cudaError_t attn_launch(const AttnArgs& a, cudaStream_t s) {
+  const int k = attn_choose(a, sm_count());
+  if (k < 0) return cudaErrorInvalidValue;
+  if (k == 2) return attn_short_launch(a, s);
   CUtensorMap tQ, tK, tV;
   const uint64_t qp = static_cast<uint64_t>(a.ldq) * 2, kp = static_cast<uint64_t>(a.ldk) * 2,
                  vp = static_cast<uint64_t>(a.ldv) * 2;

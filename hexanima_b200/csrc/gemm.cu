@@ -1109,9 +1109,11 @@ static cudaError_t launch_fmt(const GemmArgs& a, const KParams& p, const CUtenso
   return cudaErrorInvalidValue;
 }
 
-cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
+// The launch decisions of gemm_launch for a GEMM on a GPU with `sms` SMs, made on the host alone (also
+// answered by hx_gemm_query). `have_scratch`: the caller's fp16 scratch can hold the expanded weights.
+cudaError_t gemm_choose(const GemmArgs& a, int sms, bool have_scratch, GemmChoice& c) {
   const DevMat* W = a.W;
-  if (!W || !a.A || a.M <= 0 || W->N <= 0 || W->K <= 0) return cudaErrorInvalidValue;
+  if (!W || !a.A || a.M <= 0 || W->N <= 0 || W->K <= 0 || sms < 2) return cudaErrorInvalidValue;
   const int N = W->N, K = W->K;
   if (K % BK || a.K1 % BK || a.K1 <= 0 || a.K1 > K || N % 32) return cudaErrorInvalidValue;
   if (a.K1 < K && (!a.A2 || a.lda2 < K - a.K1)) return cudaErrorInvalidValue;
@@ -1125,6 +1127,7 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
     return cudaErrorInvalidValue;
   if (W->fmt == WF_Q8 && W->group != 32 && W->group != 64) return cudaErrorInvalidValue;
   if ((W->fmt == WF_Q4 || W->fmt == WF_Q4A) && W->group != 32) return cudaErrorInvalidValue;
+  c = GemmChoice();
 
   // Quantised weights with enough rows to amortise it: expand W to fp16 in the caller's scratch (one
   // memory-bound pass, 3 bytes per q8 weight), then run the fp16 kernels, which move no raw tile or
@@ -1132,22 +1135,9 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   // the q8 GEMMs run 12-21 % faster this way; the pass costs about N K 3 bytes of HBM / L2 traffic, so
   // it pays from about two images (3072 rows) up.
   if (W->fmt != WF_F16 && a.tile != 3 && (a.tile == 4 || (a.tile == 0 && a.M >= expand_min_rows()))) {
-    const size_t need = static_cast<size_t>(N) * K * 2;
-    if (a.wexp && a.wexp_bytes >= need) {
-      cudaError_t e = expand_launch(*W, a.wexp, s);
-      if (e != cudaSuccess) return e;
-      DevMat f;
-      f.fmt = WF_F16;
-      f.N = N;
-      f.K = K;
-      f.group = 64;
-      f.w = a.wexp;
-      GemmArgs b = a;
-      b.W = &f;
-      b.tile = 0;
-      b.wexp = nullptr;
-      b.wexp_bytes = 0;
-      return gemm_launch(b, s);
+    if (have_scratch) {
+      c.expand = true;
+      return cudaSuccess;  // the fp16 GEMM that follows is chosen for fp16 weights and tile 0
     }
     if (a.tile == 4) return cudaErrorInvalidValue;  // forced, but no scratch of N K fp16
   }
@@ -1155,31 +1145,36 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
   // tile configuration: CTA pairs (256x256 per cluster) unless single-CTA 128x256 tiles need fewer waves
   // (a pair moves half the weight tile per SM, so at equal waves it is the faster of the two: at one
   // image the down projection runs 67 us in pairs against 86 us in single CTAs)
+  const int npairs = sms / 2;
   const int pair_tiles = ((a.M + 2 * HALF - 1) / (2 * HALF)) * ((N + BN - 1) / BN);
   // residual GEMMs with a long K and fewer than two waves of pair tiles take the stream-K schedule below
-  const bool streamk_candidate = a.epi == EPI_RESID && a.max_ctas == 0 && pair_tiles < sm_count() &&
-                                 static_cast<long long>(pair_tiles % (sm_count() / 2)) * (K / BK) >=
-                                     32LL * (sm_count() / 2);
+  const bool streamk_candidate = a.epi == EPI_RESID && a.max_ctas == 0 && pair_tiles < sms &&
+                                 static_cast<long long>(pair_tiles % npairs) * (K / BK) >= 32LL * npairs;
 
   // q8 weights below the expansion threshold: the kernel that keeps the dequantised weights in TMEM takes
   // the RMS (q/k/v projection) epilogue when its tiles fill the GPU (2-3 % faster there than the CTA-pair
   // kernel, which is 3-7 % faster with the store, GELU and residual epilogues at several waves)
-  if (a.tile == 3) return gemm_wt_launch(a, s);
+  if (a.tile == 3) {
+    if (!gemm_wt_eligible(a)) return cudaErrorInvalidValue;
+    c.kernel = 3;
+    return cudaSuccess;
+  }
   if (a.tile == 0 && gemm_wt_eligible(a)) {
-    const int wt_tiles = gemm_wt_tiles(a), npairs = sm_count() / 2;
-    if (a.epi == EPI_RMS && wt_tiles >= npairs) return gemm_wt_launch(a, s);
+    const int wt_tiles = gemm_wt_tiles(a);
     // at most one wave of tiles with a residual or RMS epilogue (the N = 2048 projections at one image):
     // each pair has a single tile, so its epilogue is not hidden behind another tile's main loop, and the
     // TMEM-weight kernel's 8 epilogue warps per CTA with double-buffered per-warp boxes drain it faster
     // than the CTA-pair kernel's 4 warps and single staging buffer (o projection at one image: 22.5
     // against 25.6 us)
-    if ((a.epi == EPI_RESID || a.epi == EPI_RMS) && wt_tiles <= npairs && a.max_ctas == 0 && !streamk_candidate)
-      return gemm_wt_launch(a, s);
+    if ((a.epi == EPI_RMS && wt_tiles >= npairs) ||
+        ((a.epi == EPI_RESID || a.epi == EPI_RMS) && wt_tiles <= npairs && a.max_ctas == 0 && !streamk_candidate)) {
+      c.kernel = 3;
+      return cudaSuccess;
+    }
   }
 
   const int single_tiles = ((a.M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  bool pair = a.tile == 2 || (a.tile == 0 && (pair_tiles + sm_count() / 2 - 1) / (sm_count() / 2) <=
-                                                 (single_tiles + sm_count() - 1) / sm_count());
+  bool pair = a.tile == 2 || (a.tile == 0 && (pair_tiles + npairs - 1) / npairs <= (single_tiles + sms - 1) / sms);
   // residual GEMMs with fewer than two waves of pair tiles (one or two images per GPU): the CTA-pair
   // kernel with a stream-K tail, so no pair idles through a mostly empty last wave (one image: 48 tiles on
   // 74 pairs; down projection 68 -> 55 us, two images 122 -> 93 us). Tiles cut between two pairs reduce-add two
@@ -1213,7 +1208,7 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
     if (ov == 224) {
       tn = 224;
     } else if (ov != BN) {
-      int np = sm_count() / 2;
+      int np = npairs;
       if (a.max_ctas > 0 && a.max_ctas / 2 < np) np = a.max_ctas / 2 > 0 ? a.max_ctas / 2 : 1;
       const long long mt = (a.M + 2 * HALF - 1) / (2 * HALF);
       const long long w256 = (mt * ((N + BN - 1) / BN) + np - 1) / np;
@@ -1221,6 +1216,39 @@ cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
       if (w224 <= w256) tn = 224;
     }
   }
+  c.kernel = pair ? 2 : 1;
+  c.tile_n = tn;
+  c.streamk = streamk;
+  c.tiles = pair ? static_cast<int>(((a.M + 2 * HALF - 1) / (2 * HALF)) * ((N + tn - 1) / tn)) : single_tiles;
+  return cudaSuccess;
+}
+
+cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s) {
+  const DevMat* W = a.W;
+  const size_t need = W ? static_cast<size_t>(W->N) * W->K * 2 : 0;
+  GemmChoice c;
+  cudaError_t ce = gemm_choose(a, sm_count(), a.wexp && a.wexp_bytes >= need, c);
+  if (ce != cudaSuccess) return ce;
+  const int N = W->N, K = W->K;
+  if (c.expand) {
+    cudaError_t e = expand_launch(*W, a.wexp, s);
+    if (e != cudaSuccess) return e;
+    DevMat f;
+    f.fmt = WF_F16;
+    f.N = N;
+    f.K = K;
+    f.group = 64;
+    f.w = a.wexp;
+    GemmArgs b = a;
+    b.W = &f;
+    b.tile = 0;
+    b.wexp = nullptr;
+    b.wexp_bytes = 0;
+    return gemm_launch(b, s);
+  }
+  if (c.kernel == 3) return gemm_wt_launch(a, s);
+  const bool pair = c.kernel == 2;
+  const int tn = c.tile_n, streamk = c.streamk;
   const uint32_t wrows = pair ? static_cast<uint32_t>(tn / 2) : BN;
 
   CUtensorMap tA, tA2, tW, tS, tMin, tX;

@@ -88,9 +88,21 @@ struct AttnArgs {
 
 cudaError_t gemm_launch(const GemmArgs& a, cudaStream_t s);
 cudaError_t attn_short_launch(const AttnArgs& a, cudaStream_t s);
+int attn_choose(const AttnArgs& a, int sms);
 // q8 GEMM with the dequantised weights in TMEM (gemm_wt.cu): STORE / GELU / RESID / RMS epilogues,
 // N a multiple of 256; gemm_launch picks it for the RMS epilogue when its tiles fill the GPU (tile 3
 // forces it)
+// what gemm_launch runs for a GEMM: kernel 1 single-CTA 128x256 tiles, 2 CTA pairs (256 x tile_n per
+// pair, stream-K tail when streamk), 3 q8 weights in TMEM; expand: quantised weights go to fp16 first and
+// the fp16 GEMM that follows is chosen for tile 0 (tiles / tile_n then belong to that GEMM)
+struct GemmChoice {
+  int kernel = 0;
+  bool expand = false;
+  int tile_n = 256;
+  int streamk = 0;
+  int tiles = 0;
+};
+cudaError_t gemm_choose(const GemmArgs& a, int sms, bool have_scratch, GemmChoice& c);
 bool gemm_wt_eligible(const GemmArgs& a);
 int gemm_wt_tiles(const GemmArgs& a);
 cudaError_t gemm_wt_launch(const GemmArgs& a, cudaStream_t s);

@@ -109,6 +109,11 @@ class hx_gemm_desc(ctypes.Structure):
                 ("tile", ctypes.c_int)]
 
 
+class hx_gemm_plan(ctypes.Structure):
+    _fields_ = [("kernel", ctypes.c_int), ("expand", ctypes.c_int), ("tile_m", ctypes.c_int),
+                ("tile_n", ctypes.c_int), ("tiles", ctypes.c_int), ("streamk", ctypes.c_int)]
+
+
 class hx_attn_desc(ctypes.Structure):
     _fields_ = [("q", ctypes.c_void_p), ("ldq", ctypes.c_int), ("q_col0", ctypes.c_int),
                 ("k", ctypes.c_void_p), ("ldk", ctypes.c_int), ("k_col0", ctypes.c_int),
@@ -159,6 +164,8 @@ _SIGS = {
     "hx_moss_sample": [_vp, _i, _ip, _i, ctypes.POINTER(_i), _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _ip],
     "hx_gemm": [_vp, ctypes.POINTER(hx_gemm_desc)],
     "hx_attention": [_vp, ctypes.POINTER(hx_attn_desc)],
+    "hx_gemm_query": [ctypes.POINTER(hx_gemm_desc), _i, ctypes.POINTER(hx_gemm_plan)],
+    "hx_attention_query": [ctypes.POINTER(hx_attn_desc), _i, _ip],
     "hx_lnmod": [_vp, _vp, _vp, _i, _i, _vp, _vp, _l, _i, _f],
     "hx_rmsmod": [_vp, _vp, _vp, _i, _i, _vp, _vp, _vp, _l, _i, _f],
     "hx_rope_anima": [_i, _i, _d, _i, _vp, _vp],
@@ -254,6 +261,35 @@ def make_mat(fmt, n, k, w, scale=None, minv=None, group=None):
     if group is None:
         group = 64 if fmt == FMT_F16 else 32
     return hx_mat(fmt, n, k, group, _ptr(w), _ptr(scale), _ptr(minv))
+
+
+# stand-in addresses for the host-side queries: 256-byte aligned, never dereferenced
+_QADDR = 1 << 20
+
+
+def gemm_query(m, n, k, fmt, epi, group=None, tile=0, sm_count=148, k1=0):
+    """What hx_gemm would run for an m x n x k GEMM (weights of format `fmt`, epilogue `epi`) on a GPU with
+    `sm_count` SMs: dict(kernel, expand, tile_m, tile_n, tiles, streamk); kernel 1 single-CTA, 2 CTA pair,
+    3 q8 weights in TMEM. Host-side only (no handle, no device)."""
+    if group is None:
+        group = 64 if fmt == FMT_F16 else 32
+    mat = hx_mat(fmt, n, k, group, _QADDR, _QADDR, _QADDR)
+    out_cols = n // 2 if epi == EPI_SITU else n
+    d = hx_gemm_desc(_QADDR, k, _QADDR if k1 else None, k - k1 if k1 else 0, m, k1, mat, epi, _QADDR, out_cols,
+                     _QADDR, n, _QADDR, 0, 0, _QADDR, _QADDR, n, n, 0, 0, None, None, 1e-6, tile)
+    plan = hx_gemm_plan()
+    _check(lib().hx_gemm_query(ctypes.byref(d), sm_count, ctypes.byref(plan)), "hx_gemm_query")
+    return {f: getattr(plan, f) for f, _ in hx_gemm_plan._fields_}
+
+
+def attention_query(batch, heads, tq, tk, kernel=0, sm_count=148, o_addr=_QADDR):
+    """The kernel hx_attention would run (1 general, 2 short-key) for these sizes; host-side only."""
+    D = 128 * heads
+    d = hx_attn_desc(_QADDR, 3 * D, 0, _QADDR, 2 * D, 0, _QADDR, 2 * D, D, o_addr, D, batch, heads, tq, tk, 0, 1.0,
+                     kernel)
+    out = ctypes.c_int32()
+    _check(lib().hx_attention_query(ctypes.byref(d), sm_count, ctypes.byref(out)), "hx_attention_query")
+    return out.value
 
 
 class Handle:

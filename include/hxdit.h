@@ -403,6 +403,18 @@ typedef struct {
 /* O = A W^T with a fused epilogue: gemm_run_geo (hexagon/mega/gemm2.c:96-137, moss gemm2.c:145-193). */
 HX_API int hx_gemm(hx_handle h, const hx_gemm_desc* d);
 
+/* What hx_gemm runs for a descriptor on a GPU with sm_count SMs, decided on the host alone (no handle,
+ * no device work; pointers are only checked for presence and alignment). The handle's expansion scratch
+ * is assumed present, as hx_gemm reserves it. HX_OK, or HX_E_ARG when hx_gemm would reject d. */
+typedef struct {
+  int kernel;     /* 1 single-CTA tiles, 2 CTA pairs (cta_group::2), 3 q8 weights dequantised into TMEM */
+  int expand;     /* 1: quantised weights expanded to fp16 first; the fields below describe the fp16 GEMM */
+  int tile_m, tile_n;  /* output tile of a CTA (kernel 1) or of a CTA pair / TMEM-weight pair (2, 3) */
+  int tiles;      /* tiles of the launch */
+  int streamk;    /* 1: the last partial wave of CTA-pair tiles is cut into stream-K shares */
+} hx_gemm_plan;
+HX_API int hx_gemm_query(const hx_gemm_desc* d, int sm_count, hx_gemm_plan* out);
+
 typedef struct {
   const void* q; int ldq, q_col0;
   const void* k; int ldk, k_col0;
@@ -418,6 +430,9 @@ typedef struct {
 /* softmax(q k^T * scale) v per head, head_dim 128: attn_run (hexagon/mega/blk.c:54-91,
  * masked moss/hexagon/mega/blk.c:54-94). Keys >= nvalid are masked (0 = none). */
 HX_API int hx_attention(hx_handle h, const hx_attn_desc* d);
+/* The kernel hx_attention runs for d on a GPU with sm_count SMs (host-side): *kernel = 1 general, 2
+ * short-key. HX_OK, or HX_E_ARG when hx_attention would reject d. */
+HX_API int hx_attention_query(const hx_attn_desc* d, int sm_count, int32_t* kernel);
 
 /* k_lnmod_s (hexagon/mega/kern.c:31-65): h16 = LN(x) * (1 + scale) + shift, eps 1e-6 by convention. */
 HX_API int hx_lnmod(hx_handle h, const float* x, void* h16, int rows, int D, const float* shift, const float* scale,
