@@ -88,3 +88,17 @@ def test_attention_routing_rules():
         rt.attention_query(1, 16, T, 300, kernel=2, sm_count=SM)
     with pytest.raises(rt.HxError):
         rt.attention_query(1, 16, T, C, kernel=3, sm_count=SM)
+
+
+def test_moss_shapes():
+    """MOSS 1 Mpx block (q4 g32, hidden 3072, MLP 12288, SiTU): 4608 tokens on one GPU expand to fp16; a
+    rank of the 8-way Ulysses split (576 tokens) dequantises in the main loop."""
+    MD, MF = 3072, 12288
+    full = rt.gemm_query(4608, 2 * MF, MD, rt.FMT_Q4, rt.EPI_SITU, group=32, sm_count=SM)
+    assert (full["expand"], full["kernel"], full["tile_n"]) == (1, PAIR, 256)
+    rank8 = rt.gemm_query(576, 2 * MF, MD, rt.FMT_Q4, rt.EPI_SITU, group=32, sm_count=SM)
+    assert (rank8["expand"], rank8["kernel"]) == (0, PAIR)
+    qkv8 = rt.gemm_query(576, 3 * MD, MD, rt.FMT_Q4, rt.EPI_RMS, group=32, sm_count=SM)
+    assert qkv8["expand"] == 0 and qkv8["kernel"] in (SINGLE, PAIR)  # the TMEM-weight kernel takes q8 only
+    # the joint attention over the whole sequence on 3 of the 24 heads: general kernel
+    assert rt.attention_query(1, 3, 4608, 4608, sm_count=SM) == 1
