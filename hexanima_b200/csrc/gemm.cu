@@ -674,7 +674,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const int t = blockIdx.x + ti * gridDim.x;
       const int m0 = tile_m(p, t) * BM, n0 = tile_n(p, t) * BN;
       const int acc = ti & 1;
-      if (!mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 106)) { ok = false; break; }
+      // the epilogue warps meet at named barrier 1 in epilogue_tile: they leave together or not at all
+      if (!bar_and(2, EPI_WARPS * 32, mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 106))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       epilogue_tile<EPI>(p, tmem + acc * BN, m0, n0, warp, lane, &tmX, out_stage);
       tc_fence_before();
@@ -912,7 +916,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int ti = 0; ok && sched.next(p, t, kb0, kb1); ++ti) {
       const int m0 = tile_m(p, t) * 2 * HALF + row0, n0 = tile_n(p, t) * TN;
       const int acc = ti & 1;
-      if (!mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 116)) { ok = false; break; }
+      // the epilogue warps meet at named barrier 1 in epilogue_tile: they leave together or not at all
+      if (!bar_and(2, EPI_WARPS * 32, mbar_wait(&tfull[acc], (ti >> 1) & 1, p.status, 116))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       epilogue_tile<EPI, TN>(p, tmem + acc * BN, m0, n0, warp, lane, &tmX, out_stage);
       tc_fence_before();

@@ -444,7 +444,11 @@ __global__ void __launch_bounds__(WT_THREADS, 1)
         if (e.gain) e.gd = e.gain[e.d];
       }
       const int par = ti & 1;
-      if (!warp_wait(&tfull[par], (ti >> 1) & 1, p.status, 137)) { ok = false; break; }
+      // the sub-group's 4 warps meet at named barrier 1 + sub: they leave together or not at all
+      if (!bar_and(3 + sub, 128, warp_wait(&tfull[par], (ti >> 1) & 1, p.status, 137))) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       // the shared columns [256,384) hold tokens [128,256) of an even tile, [0,128) of an odd one
       const int hot_tok = tok_base + (par ? 0 : 128) + 64 * sub;
